@@ -1,0 +1,574 @@
+// liblncc_sm100: fused 3-D LNCC loss + dL/dpred for B200 (sm_100a).
+//
+// One kernel launch reads pred and target once and produces both the cc partial sums and the
+// gradient. The reference needs two kernels, four fp32 maps and two torch ops for the same result:
+// lncc_fwd (fused_lncc/csrc/lncc3d.cu:25-110), lncc_bwd (lncc3d.cu:166-235), `ncc.mean()` and
+// `* (-grad_out/M)` (fused_lncc/__init__.py:62,73).
+//
+// Sweep design (lncc_sweep_kernel). A thread block owns a TH x TW tile of output columns (H, W) of one
+// volume and walks along D through a chunk of output planes. Per input plane j it runs:
+//   A  D-pass   : running sums along D of p, t, p*p, t*t, p*t at every footprint column
+//                 ((TH+4r) x (TW+4r)), using a k-deep ring of raw planes in shared memory;
+//   B  H-pass   : box along H of those five fields        -> (TH+2r) x (TW+4r)
+//   C  W-pass   : box along W -> the five k^3 window sums at stat plane j-r on (TH+2r) x (TW+2r),
+//                 then cc (summed into the block's loss partial) and the three adjoint fields;
+//   D  H-pass   : box along H of the adjoints             -> TH x (TW+2r)
+//   E  W-pass + D running sum (k-deep ring of boxed adjoint planes) -> the adjoint box at output
+//                 plane j-2r on TH x TW, combined with p, t into dL/dpred.
+// Nothing but the gradient and one fp64 partial per block reaches global memory.
+//
+// The adjoint fields are kept in a scaled form (u = cross/(var_p*var_t)):
+//   c' = u, b' = u*u*var_t, a' = St*u - Sp*b'   so that (reference lncc3d.cu:101-104)
+//   Cc = 2c', Bc = -b', A = -(2/n)a', and d(sum cc)/dp = 2*(t*box(c') - p*box(b') - box(a')/n).
+#include "lncc.h"
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <atomic>
+#include <mutex>
+
+#define LNCC_VERSION_NUM 100  // 0.1.0
+
+namespace lncc {
+
+// ------------------------------------------------------------------------------------------------
+// element access
+// ------------------------------------------------------------------------------------------------
+template <typename S> __device__ __forceinline__ float ldf(const S* p);
+template <> __device__ __forceinline__ float ldf<float>(const float* p) { return __ldg(p); }
+template <> __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(__ldg(p));
+}
+template <typename S> __device__ __forceinline__ void stg(S* p, float v);
+template <> __device__ __forceinline__ void stg<float>(float* p, float v) { *p = v; }
+template <> __device__ __forceinline__ void stg<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+
+// ------------------------------------------------------------------------------------------------
+// geometry of the sweep kernel (all in fp32 words of shared memory)
+// ------------------------------------------------------------------------------------------------
+template <int R, int TH, int TW, int NT>
+struct SweepCfg {
+  static constexpr int K = 2 * R + 1;
+  static constexpr int W0 = TW + 4 * R, H0 = TH + 4 * R, F0 = W0 * H0;  // raw footprint
+  static constexpr int W1 = TW + 2 * R, H1 = TH + 2 * R, F1 = W1 * H1;  // stat positions
+  static constexpr int F2 = TH * TW;                                    // outputs
+  static constexpr int PPT = (F0 + NT - 1) / NT;                        // footprint columns per thread
+  static constexpr int OFF_RING = 0;                        // [K][2][F0] raw p, t planes
+  static constexpr int OFF_DS = OFF_RING + K * 2 * F0;      // [5][F0]    D-window sums
+  static constexpr int OFF_HS = OFF_DS + 5 * F0;            // [5][H1][W0] after the H box
+  static constexpr int OFF_ADJ = OFF_HS + 5 * H1 * W0;      // [3][H1][W1] adjoints at stat plane
+  static constexpr int OFF_AH = OFF_ADJ + 3 * F1;           // [3][TH][W1] adjoints after H box
+  static constexpr int OFF_RING2 = OFF_AH + 3 * TH * W1;    // [K][3][F2] HW-boxed adjoint planes
+  static constexpr int OFF_RED = (OFF_RING2 + K * 3 * F2 + 3) & ~3;  // NT/32 doubles
+  static constexpr int NWORDS = OFF_RED + 2 * (NT / 32);
+  static constexpr size_t SMEM_BYTES = size_t(NWORDS) * 4;
+  // W-pass (phase C) run length: largest of 4,3,2,1 dividing W1
+  static constexpr int M1 = (W1 % 4 == 0) ? 4 : (W1 % 3 == 0) ? 3 : (W1 % 2 == 0) ? 2 : 1;
+  static_assert(F2 <= NT * 2, "phase E maps at most two outputs per thread");
+};
+
+struct SweepArgs {
+  const void* p;
+  const void* t;
+  void* g;
+  double* partials;
+  const float* gscale_dev;
+  float gscale;  // multiplies d(sum cc)/dp
+  float inv_n;
+  float dr;
+  int D, H, W;
+  int z_begin, z_end, dchunk;
+  int tiles_w, tiles_h, nchunks;
+};
+
+template <int R, int TH, int TW, int NT, typename S, bool GRAD>
+__global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
+  using C = SweepCfg<R, TH, TW, NT>;
+  constexpr int K = C::K, W0 = C::W0, F0 = C::F0, W1 = C::W1, H1 = C::H1, F1 = C::F1, F2 = C::F2;
+  constexpr int PPT = C::PPT;
+  extern __shared__ __align__(16) float sm[];
+  float* ring = sm + C::OFF_RING;
+  float* DS = sm + C::OFF_DS;
+  float* HS = sm + C::OFF_HS;
+  float* ADJ = sm + C::OFF_ADJ;
+  float* AH = sm + C::OFF_AH;
+  float* ring2 = sm + C::OFF_RING2;
+  double* red = reinterpret_cast<double*>(sm + C::OFF_RED);
+
+  const int tid = threadIdx.x;
+  int bid = blockIdx.x;
+  const int tw = bid % a.tiles_w;
+  bid /= a.tiles_w;
+  const int th = bid % a.tiles_h;
+  bid /= a.tiles_h;
+  const int ch = bid % a.nchunks;
+  const int64_t b = bid / a.nchunks;
+  const int x0 = tw * TW, y0 = th * TH;
+  const int zs = a.z_begin + ch * a.dchunk;
+  const int ze = min(zs + a.dchunk, a.z_end);
+  const int D = a.D, H = a.H, W = a.W;
+  const int64_t HW = int64_t(H) * W;
+  const S* __restrict__ P = reinterpret_cast<const S*>(a.p) + b * D * HW;
+  const S* __restrict__ T = reinterpret_cast<const S*>(a.t) + b * D * HW;
+  S* __restrict__ G = nullptr;
+  if (GRAD) G = reinterpret_cast<S*>(a.g) + b * int64_t(a.z_end - a.z_begin) * HW;
+  const float inv_n = a.inv_n, dr = a.dr;
+  float gs = 0.f;
+  if (GRAD) gs = 2.f * a.gscale * (a.gscale_dev ? __ldg(a.gscale_dev) : 1.f);
+
+  for (int i = tid; i < K * 2 * F0; i += NT) ring[i] = 0.f;
+  if (GRAD)
+    for (int i = tid; i < K * 3 * F2; i += NT) ring2[i] = 0.f;
+
+  // phase A ownership: footprint column q = tid + i*NT
+  int aoff[PPT];
+  bool aval[PPT];
+#pragma unroll
+  for (int i = 0; i < PPT; ++i) {
+    const int q = tid + i * NT;
+    const int r0 = q / W0, c0 = q % W0;
+    const int gy = y0 - 2 * R + r0, gx = x0 - 2 * R + c0;
+    aval[i] = (q < F0) && gy >= 0 && gy < H && gx >= 0 && gx < W;
+    aoff[i] = aval[i] ? gy * W + gx : 0;
+  }
+  float s5[PPT][5];
+  float np_[PPT], nt_[PPT];
+#pragma unroll
+  for (int i = 0; i < PPT; ++i) {
+#pragma unroll
+    for (int f = 0; f < 5; ++f) s5[i][f] = 0.f;
+  }
+  const int j0 = zs - 2 * R, j1 = ze + 2 * R;
+  auto load_plane = [&](int j) {
+    const bool pv = (j >= 0) && (j < D);
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+      np_[i] = 0.f;
+      nt_[i] = 0.f;
+      if (pv && aval[i]) {
+        np_[i] = ldf<S>(P + int64_t(j) * HW + aoff[i]);
+        nt_[i] = ldf<S>(T + int64_t(j) * HW + aoff[i]);
+      }
+    }
+  };
+  load_plane(j0);
+
+  // phase E ownership (one or two outputs per thread)
+  constexpr int E_PER = (F2 + NT - 1) / NT;
+  float T3[E_PER][3];
+#pragma unroll
+  for (int e = 0; e < E_PER; ++e) T3[e][0] = T3[e][1] = T3[e][2] = 0.f;
+
+  float acc = 0.f;  // this thread's share of sum(cc)
+  __syncthreads();
+
+  for (int j = j0, it = 0; j < j1; ++j, ++it) {
+    const int slot = it % K;
+    // ---- A: D running sums at every footprint column --------------------------------------------
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+      const int q = tid + i * NT;
+      if (q < F0) {
+        const float op = ring[(slot * 2 + 0) * F0 + q];
+        const float ot = ring[(slot * 2 + 1) * F0 + q];
+        const float p = np_[i], t = nt_[i];
+        s5[i][0] += p - op;
+        s5[i][1] += t - ot;
+        s5[i][2] = fmaf(p, p, fmaf(-op, op, s5[i][2]));
+        s5[i][3] = fmaf(t, t, fmaf(-ot, ot, s5[i][3]));
+        s5[i][4] = fmaf(p, t, fmaf(-op, ot, s5[i][4]));
+        ring[(slot * 2 + 0) * F0 + q] = p;
+        ring[(slot * 2 + 1) * F0 + q] = t;
+#pragma unroll
+        for (int f = 0; f < 5; ++f) DS[f * F0 + q] = s5[i][f];
+      }
+    }
+    if (j + 1 < j1) load_plane(j + 1);
+    if (j < zs) {  // warm-up: the D sums are not complete yet
+      __syncthreads();
+      continue;
+    }
+    __syncthreads();
+    const int c1 = j - R;  // stat plane produced in this step
+    const bool c1_in = (c1 >= 0) && (c1 < D);
+    // ---- B: H box of the five D sums: (H1 x W0) ---------------------------------------------------
+    if (c1_in) {
+      for (int task = tid; task < 5 * W0; task += NT) {
+        const int f = task / W0, c = task % W0;
+        const float* src = DS + f * F0 + c;
+        float* dst = HS + f * H1 * W0 + c;
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < 2 * R + 1; ++d) s += src[d * W0];
+        dst[0] = s;
+        for (int r = 1; r < H1; ++r) {
+          s += src[(r + 2 * R) * W0] - src[(r - 1) * W0];
+          dst[r * W0] = s;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- C: W box -> window sums -> cc, adjoints at the stat plane ---------------------------------
+    {
+      constexpr int M1 = C::M1, NSEG = W1 / M1;
+      const bool c1_own = c1_in && (c1 >= zs) && (c1 < ze);
+      for (int task = tid; c1_in && task < H1 * NSEG; task += NT) {
+        const int r = task / NSEG, cs = (task % NSEG) * M1;
+        float st5[5][M1];
+#pragma unroll
+        for (int f = 0; f < 5; ++f) {
+          const float* src = HS + f * H1 * W0 + r * W0 + cs;
+          float s = 0.f;
+#pragma unroll
+          for (int d = 0; d < 2 * R + 1; ++d) s += src[d];
+          st5[f][0] = s;
+#pragma unroll
+          for (int m = 1; m < M1; ++m) {
+            s += src[m + 2 * R] - src[m - 1];
+            st5[f][m] = s;
+          }
+        }
+        const int gy = y0 - R + r;
+        const bool row_in = c1_in && gy >= 0 && gy < H;
+        const bool row_own = c1_own && (r >= R) && (r < R + TH) && (gy < H);
+#pragma unroll
+        for (int m = 0; m < M1; ++m) {
+          const int c = cs + m;
+          const int gx = x0 - R + c;
+          const bool in = row_in && gx >= 0 && gx < W;
+          const float Sp = st5[0][m], St = st5[1][m], Spp = st5[2][m], Stt = st5[3][m], Spt = st5[4][m];
+          const float ap = Sp * inv_n, at = St * inv_n;
+          const float cross = fmaf(-ap, St, Spt);
+          const float vp = fmaxf(fmaf(-ap, Sp, Spp), 0.f) + dr;
+          const float vt = fmaxf(fmaf(-at, St, Stt), 0.f) + dr;
+          const float inv = __frcp_rn(vp * vt);
+          const float u = cross * inv;
+          const float cc = cross * u;
+          if (in && row_own && c >= R && c < R + TW && gx < W) acc += (cc >= 1.f) ? 1.f : cc;
+          if (GRAD) {
+            const bool live = in && (cc < 1.f);  // NaN and cc >= 1 give zero adjoints (lncc3d.cu:100-107)
+            const float bq = u * u * vt;
+            const float aq = fmaf(St, u, -Sp * bq);
+            ADJ[0 * F1 + r * W1 + c] = live ? aq : 0.f;
+            ADJ[1 * F1 + r * W1 + c] = live ? bq : 0.f;
+            ADJ[2 * F1 + r * W1 + c] = live ? u : 0.f;
+          }
+        }
+      }
+      if (GRAD && !c1_in) {
+        for (int i = tid; i < 3 * F1; i += NT) ADJ[i] = 0.f;
+      }
+    }
+    if (!GRAD) {
+      __syncthreads();
+      continue;
+    }
+    __syncthreads();
+    // ---- D: H box of the adjoints: (TH x W1) ------------------------------------------------------
+    {
+      constexpr int SEGH = (TH % 2 == 0) ? 2 : 1, LH = TH / SEGH;
+      for (int task = tid; task < 3 * W1 * SEGH; task += NT) {
+        const int f = task / (W1 * SEGH), rem = task % (W1 * SEGH);
+        const int c = rem % W1, r0 = (rem / W1) * LH;
+        const float* src = ADJ + f * F1 + c;
+        float* dst = AH + f * TH * W1 + c;
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < 2 * R + 1; ++d) s += src[(r0 + d) * W1];
+        dst[r0 * W1] = s;
+#pragma unroll
+        for (int r = r0 + 1; r < r0 + LH; ++r) {
+          s += src[(r + 2 * R) * W1] - src[(r - 1) * W1];
+          dst[r * W1] = s;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- E: W box, D running sum, combine ----------------------------------------------------------
+    {
+      const int slot2 = it % K;       // ring2 slot of stat plane c1 (and of c1 - K)
+      const int pslot = (it + 1) % K;  // raw slot of output plane j - 2R
+      const int c2 = j - 2 * R;
+      const bool c2_out = (c2 >= zs) && (c2 < ze);
+#pragma unroll
+      for (int e = 0; e < E_PER; ++e) {
+        const int q = tid + e * NT;
+        if (q < F2) {
+          const int r = q / TW, c = q % TW;
+          float v[3];
+#pragma unroll
+          for (int f = 0; f < 3; ++f) {
+            const float* src = AH + f * TH * W1 + r * W1 + c;
+            float s = 0.f;
+#pragma unroll
+            for (int d = 0; d < 2 * R + 1; ++d) s += src[d];
+            v[f] = s;
+            float* rs = ring2 + (slot2 * 3 + f) * F2 + q;
+            T3[e][f] += s - *rs;
+            *rs = s;
+          }
+          const int gy = y0 + r, gx = x0 + c;
+          if (c2_out && gy < H && gx < W) {
+            const int q0 = (r + 2 * R) * W0 + (c + 2 * R);
+            const float p = ring[(pslot * 2 + 0) * F0 + q0];
+            const float t = ring[(pslot * 2 + 1) * F0 + q0];
+            const float gval = gs * (fmaf(t, T3[e][2], -p * T3[e][1]) - T3[e][0] * inv_n);
+            stg<S>(G + int64_t(c2 - a.z_begin) * HW + gy * W + gx, gval);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- block partial of sum(cc), fixed order ---------------------------------------------------------
+  double dacc = acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dacc += __shfl_down_sync(0xffffffffu, dacc, o);
+  if ((tid & 31) == 0) red[tid >> 5] = dacc;
+  __syncthreads();
+  if (tid == 0) {
+    double s = 0.0;
+    for (int w = 0; w < NT / 32; ++w) s += red[w];
+    a.partials[blockIdx.x] = s;
+  }
+}
+
+// Deterministic second pass: one block sums the per-block partials in a fixed order.
+__global__ void __launch_bounds__(1024) lncc_reduce_kernel(const double* __restrict__ partials, int n,
+                                                           double* sum_out, float* loss_out,
+                                                           double count) {
+  __shared__ double sh[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += partials[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += sh[w];
+    if (sum_out) *sum_out = tot;
+    if (loss_out) *loss_out = float(1.0 - tot / count);
+  }
+}
+
+template <typename S>
+__global__ void lncc_scale_grad_kernel(S* __restrict__ g, int64_t n, const float* __restrict__ go) {
+  const float s = __ldg(go);
+  if (s == 1.f) return;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    float v;
+    if constexpr (sizeof(S) == 4) v = g[i];
+    else v = __bfloat162float(g[i]);
+    stg<S>(g + i, v * s);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+constexpr int kTH = 16, kTW = 16, kNT = 256;
+
+struct Plan {
+  int R;
+  int tiles_w, tiles_h, nchunks, dchunk;
+  int64_t nblocks;
+};
+
+static int sm_count_current() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+static Plan make_plan(int64_t B, int64_t H, int64_t W, int k, int64_t z_begin, int64_t z_end) {
+  Plan pl;
+  pl.R = k / 2;
+  pl.tiles_w = int((W + kTW - 1) / kTW);
+  pl.tiles_h = int((H + kTH - 1) / kTH);
+  const int64_t nout = z_end - z_begin;
+  const int64_t base = B * pl.tiles_w * pl.tiles_h;
+  const int64_t target = 4LL * sm_count_current();
+  int64_t nch = 1;
+  if (base < target) nch = (target + base - 1) / base;
+  const int64_t min_chunk = 16;
+  int64_t maxch = (nout + min_chunk - 1) / min_chunk;
+  if (maxch < 1) maxch = 1;
+  if (nch > maxch) nch = maxch;
+  int64_t dch = (nout + nch - 1) / nch;
+  nch = (nout + dch - 1) / dch;
+  pl.nchunks = int(nch);
+  pl.dchunk = int(dch);
+  pl.nblocks = base * nch;
+  return pl;
+}
+
+template <int R, typename S, bool GRAD>
+static cudaError_t launch_sweep(const SweepArgs& a, int64_t nblocks, cudaStream_t st) {
+  using C = SweepCfg<R, kTH, kTW, kNT>;
+  auto kfn = lncc_sweep_kernel<R, kTH, kTW, kNT, S, GRAD>;
+  // The opt-in shared memory size is a per-device function attribute: set it once per device.
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kfn<<<dim3(unsigned(nblocks)), dim3(kNT), C::SMEM_BYTES, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename S, bool GRAD>
+static cudaError_t dispatch_r(int R, const SweepArgs& a, int64_t nblocks, cudaStream_t st) {
+  switch (R) {
+    case 1: return launch_sweep<1, S, GRAD>(a, nblocks, st);
+    case 2: return launch_sweep<2, S, GRAD>(a, nblocks, st);
+    case 3: return launch_sweep<3, S, GRAD>(a, nblocks, st);
+    case 4: return launch_sweep<4, S, GRAD>(a, nblocks, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static size_t smem_needed(int R) {
+  switch (R) {
+    case 1: return SweepCfg<1, kTH, kTW, kNT>::SMEM_BYTES;
+    case 2: return SweepCfg<2, kTH, kTW, kNT>::SMEM_BYTES;
+    case 3: return SweepCfg<3, kTH, kTW, kNT>::SMEM_BYTES;
+    case 4: return SweepCfg<4, kTH, kTW, kNT>::SMEM_BYTES;
+    default: return 0;
+  }
+}
+
+static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
+
+}  // namespace lncc
+
+using namespace lncc;
+
+extern "C" {
+
+const char* lncc_strerror(int status) {
+  switch (status) {
+    case LNCC_OK: return "ok";
+    case LNCC_ERR_BAD_ARG: return "fused_lncc: bad argument (null pointer, size or plane range)";
+    case LNCC_ERR_KERNEL_SIZE: return "fused_lncc: kernel_size not supported (odd 3..9)";
+    case LNCC_ERR_DTYPE: return "fused_lncc: float32 or bfloat16 only";
+    case LNCC_ERR_LAUNCH: return "fused_lncc: kernel launch failed";
+    case LNCC_ERR_SMEM: return "fused_lncc: shared memory need exceeds this GPU's opt-in cap";
+    case LNCC_ERR_WORKSPACE: return "fused_lncc: workspace missing or too small";
+    case LNCC_ERR_CUDA: return "fused_lncc: CUDA runtime error";
+    case LNCC_ERR_TOO_LARGE: return "fused_lncc: size exceeds the fixed maximum of this entry point";
+    default: return "fused_lncc: unknown status";
+  }
+}
+
+int lncc_version(void) { return LNCC_VERSION_NUM; }
+
+size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, int dtype,
+                            int64_t z_begin, int64_t z_end) {
+  (void)dtype;
+  if (B < 1 || D < 1 || H < 1 || W < 1 || !valid_k(kernel_size)) return 0;
+  if (z_begin < 0 || z_end > D || z_end <= z_begin) return 0;
+  const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
+  return size_t(pl.nblocks) * sizeof(double);
+}
+
+int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                       int64_t W, int kernel_size, float smooth_dr, int64_t z_begin, int64_t z_end,
+                       void* grad, float grad_scale, const float* grad_scale_dev, double* cc_sum_out,
+                       float* loss_out, double loss_count, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream) {
+  if (!valid_k(kernel_size)) return LNCC_ERR_KERNEL_SIZE;
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!pred || !target) return LNCC_ERR_BAD_ARG;
+  if (B < 1 || D < 1 || H < 1 || W < 1) return LNCC_ERR_BAD_ARG;
+  if (z_begin < 0 || z_end > D || z_end <= z_begin) return LNCC_ERR_BAD_ARG;
+  if (D > INT32_MAX / 2 || H * W > INT32_MAX) return LNCC_ERR_TOO_LARGE;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (grad && uintptr_t(grad) % esz))
+    return LNCC_ERR_BAD_ARG;
+  const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
+  if (pl.nblocks > INT32_MAX) return LNCC_ERR_TOO_LARGE;
+  const size_t need = size_t(pl.nblocks) * sizeof(double);
+  if (!workspace || workspace_bytes < need || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
+  if (loss_out && !(loss_count > 0.0)) return LNCC_ERR_BAD_ARG;
+
+  int dev = 0, cap = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return LNCC_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return LNCC_ERR_CUDA;
+  if (smem_needed(pl.R) > size_t(cap)) return LNCC_ERR_SMEM;
+
+  SweepArgs a;
+  a.p = pred;
+  a.t = target;
+  a.g = grad;
+  a.partials = reinterpret_cast<double*>(workspace);
+  a.gscale_dev = grad_scale_dev;
+  a.gscale = grad_scale;
+  const double n = double(kernel_size) * kernel_size * kernel_size;
+  a.inv_n = float(1.0 / n);
+  a.dr = smooth_dr;
+  a.D = int(D);
+  a.H = int(H);
+  a.W = int(W);
+  a.z_begin = int(z_begin);
+  a.z_end = int(z_end);
+  a.dchunk = pl.dchunk;
+  a.tiles_w = pl.tiles_w;
+  a.tiles_h = pl.tiles_h;
+  a.nchunks = pl.nchunks;
+
+  cudaError_t e;
+  const bool g = grad != nullptr;
+  if (dtype == LNCC_F32)
+    e = g ? dispatch_r<float, true>(pl.R, a, pl.nblocks, stream)
+          : dispatch_r<float, false>(pl.R, a, pl.nblocks, stream);
+  else
+    e = g ? dispatch_r<__nv_bfloat16, true>(pl.R, a, pl.nblocks, stream)
+          : dispatch_r<__nv_bfloat16, false>(pl.R, a, pl.nblocks, stream);
+  if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
+  if (cc_sum_out || loss_out) {
+    lncc_reduce_kernel<<<1, 1024, 0, stream>>>(a.partials, int(pl.nblocks), cc_sum_out, loss_out,
+                                               loss_count > 0.0 ? loss_count : 1.0);
+    if (cudaGetLastError() != cudaSuccess) return LNCC_ERR_LAUNCH;
+  }
+  return LNCC_OK;
+}
+
+int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!grad || !grad_out_dev || n < 0) return LNCC_ERR_BAD_ARG;
+  if (n == 0) return LNCC_OK;
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  const int64_t cap = 8LL * sm_count_current();
+  if (blocks > cap) blocks = cap;
+  if (dtype == LNCC_F32)
+    lncc_scale_grad_kernel<float><<<unsigned(blocks), threads, 0, stream>>>(
+        reinterpret_cast<float*>(grad), n, grad_out_dev);
+  else
+    lncc_scale_grad_kernel<__nv_bfloat16><<<unsigned(blocks), threads, 0, stream>>>(
+        reinterpret_cast<__nv_bfloat16*>(grad), n, grad_out_dev);
+  return cudaGetLastError() == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+}  // extern "C"

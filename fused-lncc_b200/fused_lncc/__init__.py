@@ -1,0 +1,171 @@
+"""Fused 3-D local (squared) normalized cross-correlation loss for B200 (sm_100a).
+
+Drop-in for the reference package (reference fused_lncc/__init__.py:77-83):
+
+    from fused_lncc import fused_lncc_loss
+    loss = fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5)   # 1 - mean(cc)
+    loss.backward()                                                        # grad for pred only
+
+Same signature, defaults, assertion errors, RuntimeErrors, fp32 scalar result and pred-dtype
+gradient as the reference. Inside, the forward is ONE kernel pass that also produces dL/dpred.
+The backward is then one tiny launch that returns immediately when grad_out == 1. The reference
+instead materialises four fp32 maps in the forward and box-sums them again in the backward
+(reference fused_lncc/__init__.py:50-74).
+"""
+import torch
+
+from . import _lib
+
+__all__ = ["fused_lncc_loss", "lncc_fused", "FusedLNCC"]
+
+_DTYPES = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16}
+
+
+def _check_pair(pred, target):
+    """The TORCH_CHECKs of reference lncc3d.cu:128-129,158 as RuntimeErrors."""
+    if not (pred.is_cuda and target.is_cuda):
+        raise RuntimeError("fused_lncc: pred and target must be CUDA tensors")
+    if pred.device != target.device:
+        raise RuntimeError("fused_lncc: pred and target must be on the same device")
+    if pred.shape != target.shape or pred.dtype != target.dtype:
+        raise RuntimeError("fused_lncc: target must match pred in shape and dtype")
+    if pred.dtype not in _DTYPES:
+        raise RuntimeError(f"fused_lncc: float32 or bfloat16 only, got {pred.dtype}")
+    if not (pred.is_contiguous() and target.is_contiguous()):
+        raise RuntimeError("fused_lncc: pred and target must be contiguous")
+    if pred.dim() < 3:
+        raise RuntimeError("fused_lncc: expect (..., D, H, W) volumes")
+
+
+def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_scale=None,
+               loss_count=None, z_range=None, cc_sum_out=None, loss_out=None, grad_scale_dev=None):
+    """Run the fused kernel once: returns (loss, grad).
+
+    pred/target: contiguous (..., D, H, W) CUDA tensors, fp32 or bf16; the leading dims are
+    flattened into B volumes (the reference's N*C reshape, fused_lncc/__init__.py:52-55).
+    grad: also produce d/dpred, scaled by grad_scale (default -1/M, i.e. of 1 - mean(cc)).
+    loss_count: divisor of the loss (default M = number of voxels produced).
+    z_range: (z_begin, z_end) output planes of every volume (default the whole volume); planes of
+             the array outside the range act as halo. grad then has z_end - z_begin planes.
+    cc_sum_out / loss_out: optional preallocated fp64 / fp32 one-element CUDA tensors.
+    Returns (loss: 0-dim fp32 tensor, grad: tensor or None).
+    """
+    _check_pair(pred, target)
+    *lead, D, H, W = pred.shape
+    B = 1
+    for s in lead:
+        B *= int(s)
+    z0, z1 = (0, D) if z_range is None else (int(z_range[0]), int(z_range[1]))
+    nout = B * (z1 - z0) * H * W
+    lib = _lib.load()
+    dt = _DTYPES[pred.dtype]
+    dev = pred.device
+    with torch.cuda.device(dev):
+        ws_bytes = lib.lncc_workspace_bytes(B, D, H, W, int(kernel_size), dt, z0, z1)
+        if ws_bytes == 0:
+            # invalid size/k/range: let the main call produce the precise status
+            ws_bytes = 8
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        g = None
+        if grad:
+            g = torch.empty((*lead, z1 - z0, H, W), dtype=pred.dtype, device=dev)
+        if loss_out is None:
+            loss_out = torch.empty((), dtype=torch.float32, device=dev)
+        if grad_scale is None:
+            grad_scale = -1.0 / max(nout, 1)
+        if loss_count is None:
+            loss_count = float(max(nout, 1))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        st = lib.lncc_fused_forward(
+            pred.data_ptr(), target.data_ptr(), dt, B, D, H, W, int(kernel_size), float(smooth_dr),
+            z0, z1, g.data_ptr() if g is not None else None, float(grad_scale),
+            grad_scale_dev.data_ptr() if grad_scale_dev is not None else None,
+            cc_sum_out.data_ptr() if cc_sum_out is not None else None, loss_out.data_ptr(),
+            float(loss_count), ws.data_ptr(), ws_bytes, stream)
+    _lib.check(st, "fused_lncc forward")
+    return loss_out, g
+
+
+def scale_grad_(grad, grad_out):
+    """In place grad *= grad_out (a 0-dim CUDA tensor); no work when grad_out == 1."""
+    lib = _lib.load()
+    go = grad_out.detach()
+    if go.dtype != torch.float32 or not go.is_contiguous() or go.device != grad.device:
+        go = go.to(device=grad.device, dtype=torch.float32).contiguous()
+    with torch.cuda.device(grad.device):
+        st = lib.lncc_scale_grad(grad.data_ptr(), _DTYPES[grad.dtype], grad.numel(), go.data_ptr(),
+                                 torch.cuda.current_stream(grad.device).cuda_stream)
+    _lib.check(st, "fused_lncc scale_grad")
+
+
+# torch.library custom ops, so torch.compile traces through without graph breaks (the reference
+# registers fused_lncc::forward/backward for the same reason, fused_lncc/__init__.py:22-46).
+@torch.library.custom_op("fused_lncc::fwd_grad", mutates_args=())
+def _fwd_grad_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float,
+                 need_grad: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    loss, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=need_grad)
+    if g is None:
+        g = pred.new_empty((0,))
+    return loss, g
+
+
+@_fwd_grad_op.register_fake
+def _(pred, target, kernel_size, smooth_dr, need_grad):
+    loss = pred.new_empty((), dtype=torch.float32)  # the loss is fp32 even for bf16 input
+    g = torch.empty_like(pred) if need_grad else pred.new_empty((0,))
+    return loss, g
+
+
+@torch.library.custom_op("fused_lncc::scale_grad_", mutates_args=("grad",))
+def _scale_grad_op(grad: torch.Tensor, grad_out: torch.Tensor) -> None:
+    scale_grad_(grad, grad_out)
+
+
+@_scale_grad_op.register_fake
+def _(grad, grad_out):
+    return None
+
+
+class FusedLNCC(torch.autograd.Function):
+    """Autograd glue (reference _FusedLNCC, fused_lncc/__init__.py:49-74).
+
+    forward: one fused pass -> (loss, dL/dpred for grad_out = 1), the gradient kept for backward.
+    backward: scales that gradient by grad_out in place and hands it over (no copy). A second
+    backward through the same graph (retain_graph=True) recomputes it from the saved inputs.
+    """
+
+    @staticmethod
+    def forward(ctx, pred, target, kernel_size, smooth_dr, need_grad=None):
+        # Grad mode is off inside forward; the caller passes whether the graph wants d/dpred.
+        if need_grad is None:
+            need_grad = bool(ctx.needs_input_grad[0])
+        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr, need_grad)
+        ctx.save_for_backward(pred, target)
+        ctx.k = kernel_size
+        ctx.dr = smooth_dr
+        ctx.grad = g if need_grad else None
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        g = ctx.grad
+        ctx.grad = None  # hand the buffer over; a later backward recomputes
+        if g is None or g.numel() == 0:
+            pred, target = ctx.saved_tensors
+            _, g = torch.ops.fused_lncc.fwd_grad(pred, target, ctx.k, ctx.dr, True)
+        torch.ops.fused_lncc.scale_grad_(g, grad_out)
+        return g, None, None, None, None
+
+
+_FusedLNCC = FusedLNCC  # the reference's private name
+
+
+def fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5):
+    """1 - mean(squared local NCC). Gradient flows through `pred` only.
+
+    pred, target: (N, C, D, H, W) fp32 or bf16 CUDA. kernel_size odd (3, 5, 7 or 9).
+    Returns a 0-dim fp32 loss in [0, 1] (reference fused_lncc/__init__.py:77-83)."""
+    assert pred.dim() == 5 and pred.shape == target.shape, "expect matching (N,C,D,H,W)"
+    assert kernel_size % 2 == 1, "kernel_size must be odd"
+    need_grad = bool(pred.requires_grad and torch.is_grad_enabled())
+    return FusedLNCC.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr, need_grad)

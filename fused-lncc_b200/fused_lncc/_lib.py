@@ -1,0 +1,78 @@
+"""ctypes binding of liblncc_sm100.so (declared in include/lncc.h).
+
+This is the extension loader. The reference imports a prebuilt pybind module or JIT-builds one
+(reference fused_lncc/__init__.py:10-19). Here the library is a plain C ABI, so any FFI can bind
+it. If it is missing and nvcc is present it is compiled in-tree once. If that fails, the import
+error propagates. There is no CPU or PyTorch fallback.
+"""
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblncc_sm100.so")
+
+LNCC_OK = 0
+LNCC_F32 = 0
+LNCC_BF16 = 1
+
+_c_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); must list every function of include/lncc.h
+SIGNATURES = {
+    "lncc_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "lncc_version": (ctypes.c_int, []),
+    "lncc_workspace_bytes": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
+                                               _c_i64, _c_i64]),
+    "lncc_fused_forward": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int,                      # pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float,                # kernel_size, smooth_dr
+        _c_i64, _c_i64,                              # z_begin, z_end
+        _vp, ctypes.c_float, _vp,                    # grad, grad_scale, grad_scale_dev
+        _vp, _vp, ctypes.c_double,                   # cc_sum_out, loss_out, loss_count
+        _vp, ctypes.c_size_t, _vp,                   # workspace, bytes, stream
+    ]),
+    "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _build_if_missing():
+    if os.path.exists(LIB_PATH):
+        return
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "_lncc_build", os.path.join(os.path.dirname(_HERE), "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build_library()
+
+
+def load():
+    """Load (building once if absent) and return the ctypes library handle."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            _build_if_missing()
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def strerror(status):
+    return load().lncc_strerror(int(status)).decode()
+
+
+def check(status, what):
+    if status != LNCC_OK:
+        raise RuntimeError(f"{what}: {strerror(status)} (status {status})")

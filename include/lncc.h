@@ -1,0 +1,99 @@
+/*
+ * lncc.h - C ABI of the B200 (sm_100a) fused 3-D LNCC loss library (liblncc_sm100.so).
+ *
+ * Every entry point is a plain C function: raw device pointers, sizes, a CUDA stream, and an int
+ * status code (LNCC_OK == 0). No C++ exception crosses this boundary and no call allocates device
+ * memory: the caller owns every buffer, including the scratch "workspace" whose size
+ * lncc_workspace_bytes() reports. All work is enqueued on the caller's stream, on the current device.
+ *
+ * Layout: pred/target/grad are contiguous (B, D, H, W) volumes, B = N*C, W fastest, fp32 or bf16.
+ *
+ * Math (reference fused_lncc/csrc/lncc3d.cu:5-8,93-108): for each voxel the k^3 zero-padded box
+ * (n = k^3 at borders too) gives Sp, St, Spp, Stt, Spt;
+ *   cross = Spt - Sp*St/n, var_p = max(Spp - Sp^2/n, 0) + dr, var_t = max(Stt - St^2/n, 0) + dr,
+ *   cc = cross^2 / (var_p*var_t), clamped to 1 (NaN propagates), loss = 1 - mean(cc).
+ * dL/dpred = -(1/M) * (box(A) + 2*pred*box(B) + target*box(C)) with the adjoints of
+ * lncc3d.cu:100-107 (all zero where cc >= 1).
+ */
+#ifndef LNCC_SM100_H
+#define LNCC_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. Mirrors the reference's TORCH_CHECK failure classes (lncc3d.cu:123,128-129,158,159). */
+enum lncc_status {
+  LNCC_OK = 0,
+  LNCC_ERR_BAD_ARG = 1,         /* null pointer, non-positive size, bad plane range */
+  LNCC_ERR_KERNEL_SIZE = 2,     /* kernel_size not in {3,5,7,9}  (lncc3d.cu:123) */
+  LNCC_ERR_DTYPE = 3,           /* dtype not fp32/bf16           (lncc3d.cu:158) */
+  LNCC_ERR_LAUNCH = 4,          /* kernel launch failed          (lncc3d.cu:159) */
+  LNCC_ERR_SMEM = 5,            /* shared memory need above the device opt-in cap (lncc3d.cu:143-148) */
+  LNCC_ERR_WORKSPACE = 6,       /* workspace missing or smaller than lncc_workspace_bytes() */
+  LNCC_ERR_CUDA = 7,            /* other CUDA runtime error */
+  LNCC_ERR_TOO_LARGE = 8        /* size beyond a stated fixed maximum */
+};
+
+/* Element types of pred / target / grad (the reference dispatches on the same two, lncc3d.cu:151-158). */
+enum lncc_dtype { LNCC_F32 = 0, LNCC_BF16 = 1 };
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* lncc_strerror(int status);
+
+/* Library version as major*10000 + minor*100 + patch. */
+int lncc_version(void);
+
+/*
+ * Bytes of scratch the fused kernel needs for a call with these sizes: one fp64 partial sum of cc
+ * per thread block. The reference allocates its four fp32 maps itself (lncc3d.cu:130-132); here the
+ * only scratch is this small partials array (a few KB to a few hundred KB).
+ * z_begin/z_end: output plane range (see lncc_fused_forward); pass 0, D for whole volumes.
+ */
+size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, int dtype,
+                            int64_t z_begin, int64_t z_end);
+
+/*
+ * One fused pass: reads pred and target once, writes the per-block cc partial sums, and (when
+ * grad != NULL) writes dL/dpred in pred's dtype. Replaces the reference's lncc_forward
+ * (lncc3d.cu:127-161) plus lncc_backward (lncc3d.cu:253-284) plus the torch `ncc.mean()` and
+ * `* (-grad_out/M)` steps of fused_lncc/__init__.py:56-73: nothing is materialised in between.
+ *
+ *   pred, target : (B, D, H, W) device arrays of `dtype`.
+ *   z_begin,z_end: only output planes [z_begin, z_end) of every volume are produced (loss terms and
+ *                  grad). Planes outside the array are zero padding; planes inside it but outside
+ *                  the range are read as halo. Whole volumes: 0, D. D-slab shards pass a slab with
+ *                  2*(k/2) halo planes on each interior side.
+ *   grad         : NULL (loss only, 8 B/voxel of traffic for fp32) or a (B, z_end-z_begin, H, W)
+ *                  array of `dtype` that receives grad_scale * (*grad_scale_dev, if not NULL) *
+ *                  d(sum cc)/dpred. For the loss 1 - mean(cc) pass grad_scale = -1/M.
+ *   cc_sum_out   : NULL or one device double receiving sum(cc) over the produced voxels.
+ *   loss_out     : NULL or one device float receiving 1 - sum(cc)/loss_count.
+ *   workspace    : device scratch of at least lncc_workspace_bytes(...) bytes (8-byte aligned).
+ * The cc sum is reduced in a fixed order: results are bitwise reproducible run to run.
+ */
+int lncc_fused_forward(const void* pred, const void* target, int dtype,
+                       int64_t B, int64_t D, int64_t H, int64_t W,
+                       int kernel_size, float smooth_dr,
+                       int64_t z_begin, int64_t z_end,
+                       void* grad, float grad_scale, const float* grad_scale_dev,
+                       double* cc_sum_out, float* loss_out, double loss_count,
+                       void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * In place grad *= *grad_out for n elements of `dtype`; every block returns at once when
+ * *grad_out == 1 (the usual loss.backward() case), so that case costs one tiny launch.
+ * Replaces the `* (-grad_out / ctx.M)` tensor multiply of fused_lncc/__init__.py:73 (the -1/M part
+ * is already folded into lncc_fused_forward's grad_scale).
+ */
+int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LNCC_SM100_H */

@@ -1,0 +1,257 @@
+"""GPU parity: the sm_100a kernels against the CPU oracle and the reference's golden vectors.
+
+Assertions mirror the reference's own suites (tests/test_pytest.py, test_robust.py, test_fixes.py,
+test_bf16.py, verify_bwd.py) at the tolerances of the port's contract:
+  fp32: |loss - oracle| < 1e-5, grad cosine > 0.9999 and relative L2 error < 1e-3;
+  bf16: |loss - oracle(bf16 values)| < 1e-3, grad relative L2 error < 1e-2.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from fused_lncc import fused_lncc_loss, lncc_fused
+from oracle import c_oracle
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FP32_LOSS_TOL = 1e-5
+FP32_COS = 0.9999
+FP32_REL = 1e-3
+BF16_LOSS_TOL = 1e-3
+BF16_REL = 1e-2
+
+
+def fused(p, t, k, dr=1e-5):
+    p = p.detach().clone().requires_grad_(True)
+    loss = fused_lncc_loss(p, t, k, dr)
+    loss.backward()
+    torch.cuda.synchronize()
+    return loss.item(), p.grad
+
+
+def oracle(p, t, k, dr=1e-5):
+    o = c_oracle.lncc(p.detach().float().cpu().numpy(), t.detach().float().cpu().numpy(), k, dr)
+    return o["loss"], torch.from_numpy(o["grad"])
+
+
+def cos_rel(g, ref):
+    g = g.detach().float().cpu().flatten().double()
+    ref = ref.detach().float().cpu().flatten().double()
+    cos = F.cosine_similarity(g, ref, dim=0).item()
+    rel = ((g - ref).norm() / ref.norm().clamp_min(1e-300)).item()
+    return cos, rel
+
+
+def assert_fp32_parity(p, t, k, loss_tol=FP32_LOSS_TOL):
+    lf, gf = fused(p, t, k)
+    lo, go = oracle(p, t, k)
+    assert abs(lf - lo) < loss_tol, (lf, lo)
+    cos, rel = cos_rel(gf, go)
+    assert cos > FP32_COS and rel < FP32_REL, (cos, rel)
+    assert gf.dtype == p.dtype and gf.shape == p.shape
+
+
+# ---- golden vectors from the reference's own oracle -------------------------------------------------
+def test_golden_cases():
+    arr = np.load(os.path.join(GOLD, "golden.npz"))
+    meta = json.load(open(os.path.join(GOLD, "golden.json")))
+    for name, c in meta["cases"].items():
+        p = torch.from_numpy(arr[name + "/pred"]).cuda()
+        t = torch.from_numpy(arr[name + "/target"]).cuda()
+        lf, gf = fused(p, t, c["k"])
+        assert abs(lf - c["loss_f64"]) < FP32_LOSS_TOL, (name, lf, c["loss_f64"])
+        cos, rel = cos_rel(gf, torch.from_numpy(arr[name + "/grad"]))
+        assert cos > FP32_COS and rel < FP32_REL, (name, cos, rel)
+
+
+def test_golden_config1():
+    from fused_lncc import synth
+    arr = np.load(os.path.join(GOLD, "golden.npz"))
+    c1 = json.load(open(os.path.join(GOLD, "golden.json")))["config1"]
+    pred, target = synth.blurred_pair((1, 1, 64, 64, 64), device="cpu")
+    assert synth.sha256_of(pred) == c1["sha256_pred"]
+    lf, gf = fused(pred.cuda(), target.cuda(), 7)
+    assert abs(lf - c1["loss_f64"]) < FP32_LOSS_TOL
+    flat = gf.cpu().flatten().double()
+    idx = torch.from_numpy(arr["config1/sample_idx"])
+    ref = torch.from_numpy(arr["config1/sample_grad"])
+    rel = ((flat[idx] - ref).norm() / ref.norm()).item()
+    assert rel < FP32_REL
+    assert abs(flat.norm().item() / c1["grad_l2"] - 1) < FP32_REL
+
+
+# ---- reference tests/test_pytest.py --------------------------------------------------------------
+@pytest.mark.parametrize("k", [3, 5, 7, 9])
+def test_forward_backward_matches_oracle(k):
+    torch.manual_seed(0)
+    p = torch.randn(2, 4, 32, 32, 32, device="cuda")
+    t = torch.randn_like(p)
+    assert_fp32_parity(p, t, k)
+
+
+def test_bf16_runs():
+    p = torch.randn(1, 2, 16, 16, 16, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    t = torch.randn_like(p)
+    loss = fused_lncc_loss(p, t, 7)
+    loss.backward()
+    assert loss.dtype == torch.float32
+    assert p.grad.dtype == torch.bfloat16 and torch.isfinite(p.grad).all()
+
+
+def test_degenerate_zero_in_range():
+    p = torch.zeros(1, 1, 16, 16, 16, device="cuda")
+    loss = fused_lncc_loss(p, p, 7)
+    assert torch.isfinite(loss) and 0.0 <= loss.item() <= 1.001
+
+
+def test_unsupported_dtype_and_kernel_raise():
+    p = torch.randn(1, 1, 16, 16, 16, device="cuda", dtype=torch.float64)
+    with pytest.raises(RuntimeError):
+        fused_lncc_loss(p, p, 7)
+    q = torch.randn(1, 1, 16, 16, 16, device="cuda")
+    with pytest.raises(RuntimeError):
+        fused_lncc_loss(q, q, 11)
+    with pytest.raises(RuntimeError):
+        fused_lncc_loss(q, q.bfloat16(), 7)
+
+
+# ---- reference tests/test_robust.py ---------------------------------------------------------------
+@pytest.mark.parametrize("k", [3, 5, 7, 9])
+def test_regression_28cube(k):
+    torch.manual_seed(0)
+    p = torch.randn(2, 4, 28, 28, 28, device="cuda")
+    t = torch.randn(2, 4, 28, 28, 28, device="cuda")
+    assert_fp32_parity(p, t, k)
+
+
+@pytest.mark.parametrize("name,p,t", [
+    ("zeros", torch.zeros(2, 2, 32, 32, 32), torch.zeros(2, 2, 32, 32, 32)),
+    ("const5", torch.full((2, 2, 32, 32, 32), 5.0), torch.full((2, 2, 32, 32, 32), 5.0)),
+    ("const1e4", torch.full((1, 1, 32, 32, 32), 1e4), torch.full((1, 1, 32, 32, 32), 1e4)),
+    ("near_const", torch.full((1, 2, 24, 24, 24), 3.0) + 1e-3 * torch.randn(1, 2, 24, 24, 24,
+                                                                             generator=torch.Generator().manual_seed(5)),
+     torch.full((1, 2, 24, 24, 24), 3.0)),
+])
+def test_degenerate_inputs(name, p, t):
+    p, t = p.cuda(), t.cuda()
+    lf, gf = fused(p, t, 7)
+    assert np.isfinite(lf) and 0.0 <= lf <= 1.0001, (name, lf)
+    assert torch.isfinite(gf).all(), name
+    lo, _ = oracle(p, t, 7)
+    assert abs(lf - lo) < 1e-3, (name, lf, lo)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 2, 2, 2), (1, 1, 2, 40, 40), (1, 3, 7, 9, 11), (3, 5, 13, 17, 19),
+                                   (1, 1, 128, 1, 1), (1, 1, 1, 1, 1), (2, 1, 1, 33, 65), (1, 1, 9, 1, 70)])
+@pytest.mark.parametrize("k", [3, 7, 9])
+def test_shape_edge_cases(shape, k):
+    g = torch.Generator().manual_seed(hash((shape, k)) % (2 ** 31))
+    p = torch.randn(*shape, generator=g).cuda()
+    t = torch.randn(*shape, generator=g).cuda()
+    assert_fp32_parity(p, t, k)
+
+
+def test_large_shape_runs():
+    p = torch.randn(2, 32, 128, 128, 128, device="cuda", requires_grad=True)
+    t = torch.randn_like(p)
+    fused_lncc_loss(p, t, 7).backward()
+    assert torch.isfinite(p.grad).all()
+
+
+# ---- reference tests/test_fixes.py ----------------------------------------------------------------
+def test_many_volumes_deep():
+    p = torch.randn(2080, 1, 128, 8, 8, device="cuda", requires_grad=True)
+    t = torch.randn_like(p)
+    loss = fused_lncc_loss(p, t, 7)
+    loss.backward()
+    assert torch.isfinite(loss) and torch.isfinite(p.grad).all()
+    # spot-check parity on a few of the volumes
+    sel = [0, 1037, 2079]
+    o = c_oracle.lncc(p.detach()[sel].cpu().numpy(), t[sel].cpu().numpy(), 7, grad_scale=-1.0 / p.numel())
+    cos, rel = cos_rel(p.grad[sel], torch.from_numpy(o["grad"]))
+    assert cos > FP32_COS and rel < FP32_REL
+
+
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_nonfinite_input_gives_nonfinite_loss(bad):
+    t = torch.randn(1, 1, 16, 16, 16, device="cuda")
+    p = torch.randn(1, 1, 16, 16, 16, device="cuda")
+    p[0, 0, 8, 8, 8] = bad
+    assert not torch.isfinite(fused_lncc_loss(p, t, 7))
+
+
+@pytest.mark.parametrize("k", [3, 5, 7, 9])
+def test_regression_40cube(k):
+    torch.manual_seed(1)
+    p = torch.randn(2, 8, 40, 40, 40, device="cuda")
+    t = torch.randn_like(p)
+    assert_fp32_parity(p, t, k)
+
+
+# ---- reference tests/test_bf16.py -----------------------------------------------------------------
+@pytest.mark.parametrize("k", [3, 7, 9])
+def test_bf16_matches_fp32_of_bf16_values(k):
+    torch.manual_seed(0)
+    pb = torch.randn(2, 4, 40, 40, 40, device="cuda", dtype=torch.bfloat16)
+    tb = torch.randn(2, 4, 40, 40, 40, device="cuda", dtype=torch.bfloat16)
+    lb, gb = fused(pb, tb, k)
+    lo, go = oracle(pb, tb, k)
+    assert abs(lb - lo) < BF16_LOSS_TOL
+    _, rel = cos_rel(gb, go)
+    assert gb.dtype == torch.bfloat16 and torch.isfinite(gb).all() and rel < BF16_REL
+
+
+# ---- autograd glue ---------------------------------------------------------------------------------
+def test_grad_out_scaling_and_retain_graph():
+    torch.manual_seed(2)
+    p = torch.randn(1, 2, 20, 20, 20, device="cuda", requires_grad=True)
+    t = torch.randn_like(p)
+    loss = fused_lncc_loss(p, t, 5)
+    (3.0 * loss).backward(retain_graph=True)
+    g1 = p.grad.clone()
+    p.grad = None
+    loss.backward()                       # second backward recomputes
+    g2 = p.grad.clone()
+    torch.testing.assert_close(g1, 3.0 * g2, rtol=1e-5, atol=1e-12)
+    lo, go = oracle(p, t, 5)
+    cos, rel = cos_rel(g2, go)
+    assert cos > FP32_COS and rel < FP32_REL
+
+
+def test_no_grad_path_loss_only():
+    torch.manual_seed(3)
+    p = torch.randn(2, 1, 24, 24, 24, device="cuda")
+    t = torch.randn_like(p)
+    with torch.no_grad():
+        l0 = fused_lncc_loss(p, t, 7).item()
+    l1, _ = fused(p, t, 7)
+    assert l0 == l1
+
+
+def test_deterministic():
+    torch.manual_seed(4)
+    p = torch.randn(2, 3, 33, 35, 37, device="cuda")
+    t = torch.randn_like(p)
+    l1, g1 = fused(p, t, 7)
+    l2, g2 = fused(p, t, 7)
+    assert l1 == l2 and torch.equal(g1, g2)
+
+
+def test_plane_range_matches_whole_volume():
+    torch.manual_seed(5)
+    p = torch.randn(2, 1, 40, 19, 23, device="cuda")
+    t = torch.randn_like(p)
+    _, g_full = lncc_fused(p, t, 7, grad_scale=1.0)
+    s_full = torch.zeros(1, dtype=torch.float64, device="cuda")
+    s_part = torch.zeros(1, dtype=torch.float64, device="cuda")
+    lncc_fused(p, t, 7, grad=False, cc_sum_out=s_full)
+    parts = 0.0
+    for z0, z1 in [(0, 13), (13, 29), (29, 40)]:
+        _, g = lncc_fused(p, t, 7, grad_scale=1.0, z_range=(z0, z1), cc_sum_out=s_part)
+        parts += s_part.item()
+        torch.testing.assert_close(g, g_full[:, :, z0:z1], rtol=1e-4, atol=1e-5)
+    assert abs(parts - s_full.item()) < 1e-6 * max(1.0, abs(s_full.item()))
