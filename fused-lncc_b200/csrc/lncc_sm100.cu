@@ -17,18 +17,24 @@
 //                 plane j-2r on TH x TW, combined with p, t into dL/dpred.
 // Nothing but the gradient and one fp64 partial per block reaches global memory.
 //
-// The adjoint fields are kept in a scaled form (u = cross/(var_p*var_t)):
-//   c' = u, b' = u*u*var_t, a' = St*u - Sp*b'   so that (reference lncc3d.cu:101-104)
-//   Cc = 2c', Bc = -b', A = -(2/n)a', and d(sum cc)/dp = 2*(t*box(c') - p*box(b') - box(a')/n).
+// Statistics are kept multiplied by n = k^3, so that constant inputs cancel exactly as with the
+// reference's division by n (lncc3d.cu:93-97):
+//   X = n*Spt - Sp*St = n*cross,  VP = max(n*Spp - Sp^2, 0) + n*dr = n*var_p,  VT likewise,
+//   cc = X^2/(VP*VT).  With w = X/(VP*VT) the adjoints of lncc3d.cu:101-104 are
+//   Cc = 2n*c, Bc = -n*b, A = -2*a  for  c = w, b = w*w*VT, a = w*(St - w*VT*Sp),
+// and d(sum cc)/dp = box(A) + 2p*box(Bc) + t*box(Cc) = 2*(n*t*box(c) - n*p*box(b) - box(a)).
 #include "lncc.h"
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <atomic>
 #include <mutex>
 
 #define LNCC_VERSION_NUM 100  // 0.1.0
+
+#include "lncc_band.cuh"
 
 namespace lncc {
 
@@ -77,7 +83,7 @@ struct SweepArgs {
   double* partials;
   const float* gscale_dev;
   float gscale;  // multiplies d(sum cc)/dp
-  float inv_n;
+  float n;       // k^3
   float dr;
   int D, H, W;
   int z_begin, z_end, dchunk;
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
   const S* __restrict__ T = reinterpret_cast<const S*>(a.t) + b * D * HW;
   S* __restrict__ G = nullptr;
   if (GRAD) G = reinterpret_cast<S*>(a.g) + b * int64_t(a.z_end - a.z_begin) * HW;
-  const float inv_n = a.inv_n, dr = a.dr;
+  const float nf = a.n, ndr = a.n * a.dr;
   float gs = 0.f;
   if (GRAD) gs = 2.f * a.gscale * (a.gscale_dev ? __ldg(a.gscale_dev) : 1.f);
 
@@ -240,21 +246,20 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
           const int gx = x0 - R + c;
           const bool in = row_in && gx >= 0 && gx < W;
           const float Sp = st5[0][m], St = st5[1][m], Spp = st5[2][m], Stt = st5[3][m], Spt = st5[4][m];
-          const float ap = Sp * inv_n, at = St * inv_n;
-          const float cross = fmaf(-ap, St, Spt);
-          const float vp = fmaxf(fmaf(-ap, Sp, Spp), 0.f) + dr;
-          const float vt = fmaxf(fmaf(-at, St, Stt), 0.f) + dr;
-          const float inv = __frcp_rn(vp * vt);
-          const float u = cross * inv;
-          const float cc = cross * u;
+          const float X = fmaf(nf, Spt, -(Sp * St));
+          const float VP = fmaxf(fmaf(nf, Spp, -(Sp * Sp)), 0.f) + ndr;
+          const float VT = fmaxf(fmaf(nf, Stt, -(St * St)), 0.f) + ndr;
+          const float w = X * __frcp_rn(VP * VT);
+          const float cc = X * w;
           if (in && row_own && c >= R && c < R + TW && gx < W) acc += (cc >= 1.f) ? 1.f : cc;
           if (GRAD) {
             const bool live = in && (cc < 1.f);  // NaN and cc >= 1 give zero adjoints (lncc3d.cu:100-107)
-            const float bq = u * u * vt;
-            const float aq = fmaf(St, u, -Sp * bq);
+            const float wv = w * VT;
+            const float bq = w * wv;
+            const float aq = w * fmaf(-wv, Sp, St);
             ADJ[0 * F1 + r * W1 + c] = live ? aq : 0.f;
             ADJ[1 * F1 + r * W1 + c] = live ? bq : 0.f;
-            ADJ[2 * F1 + r * W1 + c] = live ? u : 0.f;
+            ADJ[2 * F1 + r * W1 + c] = live ? w : 0.f;
           }
         }
       }
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
             const int q0 = (r + 2 * R) * W0 + (c + 2 * R);
             const float p = ring[(pslot * 2 + 0) * F0 + q0];
             const float t = ring[(pslot * 2 + 1) * F0 + q0];
-            const float gval = gs * (fmaf(t, T3[e][2], -p * T3[e][1]) - T3[e][0] * inv_n);
+            const float gval = gs * fmaf(nf, fmaf(t, T3[e][2], -p * T3[e][1]), -T3[e][0]);
             stg<S>(G + int64_t(c2 - a.z_begin) * HW + gy * W + gx, gval);
           }
         }
@@ -459,6 +464,162 @@ static size_t smem_needed(int R) {
 
 static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
 
+// ------------------------------------------------------------------------------------------------
+// band kernel host side
+// ------------------------------------------------------------------------------------------------
+static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band
+
+// Row segments per column in the band kernel's column phases (threads = 128 * segments).
+// LNCC_BAND_SEGMENTS=2|4 overrides the default (a tuning knob; both variants compute the same).
+static int band_segments() {
+  static const int v = [] {
+    const char* e = getenv("LNCC_BAND_SEGMENTS");
+    const int x = e ? atoi(e) : 4;
+    return (x == 2 || x == 4) ? x : 4;
+  }();
+  return v;
+}
+
+template <int R, typename S, bool GRAD, int NSEG>
+static cudaError_t band_prepare(const void** fn_out) {
+  auto kfn = band::lncc_band_kernel<R, S, GRAD, NSEG>;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, band::smem_bytes<R>());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  *fn_out = reinterpret_cast<const void*>(kfn);
+  return cudaSuccess;
+}
+
+template <typename S, bool GRAD, int NSEG>
+static cudaError_t band_fn_seg(int R, const void** fn) {
+  switch (R) {
+    case 1: return band_prepare<1, S, GRAD, NSEG>(fn);
+    case 2: return band_prepare<2, S, GRAD, NSEG>(fn);
+    case 3: return band_prepare<3, S, GRAD, NSEG>(fn);
+    case 4: return band_prepare<4, S, GRAD, NSEG>(fn);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename S, bool GRAD>
+static cudaError_t band_fn(int R, const void** fn) {
+  return band_segments() == 2 ? band_fn_seg<S, GRAD, 2>(R, fn) : band_fn_seg<S, GRAD, 4>(R, fn);
+}
+
+static cudaError_t band_kernel_fn(int R, int dtype, bool grad, const void** fn) {
+  if (dtype == LNCC_F32) return grad ? band_fn<float, true>(R, fn) : band_fn<float, false>(R, fn);
+  return grad ? band_fn<__nv_bfloat16, true>(R, fn) : band_fn<__nv_bfloat16, false>(R, fn);
+}
+
+static bool band_supported(int64_t H, int64_t W, int dtype, const void* p, const void* t, const void* g) {
+  if (W > band::WMAX || (W % 4) != 0) return false;
+  if (H > int64_t(band::TH) * 16) return false;
+  const uintptr_t al = dtype == LNCC_F32 ? 16 : 8;
+  if ((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al))) return false;
+  return true;
+}
+
+// Number of clusters that fit on the device at once (cached per device / cluster size / variant).
+static int band_smem_for(int R) {
+  switch (R) {
+    case 1: return band::smem_bytes<1>();
+    case 2: return band::smem_bytes<2>();
+    case 3: return band::smem_bytes<3>();
+    default: return band::smem_bytes<4>();
+  }
+}
+
+static int band_max_clusters(const void* fn, int cy, int cy_r) {
+  static std::mutex mu;
+  struct Key { int dev; int cy; const void* fn; int val; };
+  static Key cache[64];
+  static int ncache = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < ncache; ++i)
+    if (cache[i].dev == dev && cache[i].cy == cy && cache[i].fn == fn) return cache[i].val;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(cy);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(unsigned(cy), 1, 1);
+  cfg.blockDim = dim3(band::NT, 1, 1);
+  cfg.dynamicSmemBytes = size_t(band_smem_for(cy_r));
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (ncache < 64) cache[ncache++] = {dev, cy, fn, n};
+  return n;
+}
+
+struct BandPlan {
+  bool ok;
+  int R;
+  int cy;
+  int64_t nclusters;
+  int64_t ppc;
+  const void* fn;
+};
+
+static BandPlan make_band_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bool grad, int64_t z_begin,
+                               int64_t z_end, const void* p, const void* t, const void* g) {
+  BandPlan bp{false, k / 2, 0, 0, 0, nullptr};
+  const int choice = g_kernel_choice.load();
+  if (choice == 1) return bp;
+  if (!band_supported(H, W, dtype, p, t, g)) return bp;
+  const void* fn = nullptr;
+  if (band_kernel_fn(k / 2, dtype, grad, &fn) != cudaSuccess) return bp;
+  const int cy = int((H + band::TH - 1) / band::TH);
+  const int maxc = band_max_clusters(fn, cy, k / 2);
+  if (maxc < 1) return bp;
+  const int64_t total = B * (z_end - z_begin);
+  const int64_t min_ppc = 32;
+  int64_t nc = (total + min_ppc - 1) / min_ppc;
+  if (nc > maxc) nc = maxc;
+  if (nc < 1) nc = 1;
+  const int64_t ppc = (total + nc - 1) / nc;
+  nc = (total + ppc - 1) / ppc;
+  bp.ok = true;
+  bp.cy = cy;
+  bp.nclusters = nc;
+  bp.ppc = ppc;
+  bp.fn = fn;
+  return bp;
+}
+
+static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(bp.cy);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(unsigned(bp.cy), unsigned(bp.nclusters), 1);
+  cfg.blockDim = dim3(band::NT, 1, 1);
+  cfg.dynamicSmemBytes = size_t(band_smem_for(bp.R));
+  cfg.stream = st;
+  void* args[] = {const_cast<band::BandArgs*>(&ba)};
+  return cudaLaunchKernelExC(&cfg, bp.fn, args);
+}
+
 }  // namespace lncc
 
 using namespace lncc;
@@ -484,11 +645,21 @@ int lncc_version(void) { return LNCC_VERSION_NUM; }
 
 size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, int dtype,
                             int64_t z_begin, int64_t z_end) {
-  (void)dtype;
   if (B < 1 || D < 1 || H < 1 || W < 1 || !valid_k(kernel_size)) return 0;
   if (z_begin < 0 || z_end > D || z_end <= z_begin) return 0;
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return 0;
+  // enough for either kernel (the choice also depends on pointer alignment, known only at launch)
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
-  return size_t(pl.nblocks) * sizeof(double);
+  size_t need = size_t(pl.nblocks) * sizeof(double);
+  const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, true, z_begin, z_end, nullptr, nullptr, nullptr);
+  if (bp.ok) {
+    const size_t nb = size_t(bp.cy) * size_t(bp.nclusters) * sizeof(double);
+    if (nb > need) need = nb;
+    const BandPlan bq = make_band_plan(B, H, W, kernel_size, dtype, false, z_begin, z_end, nullptr, nullptr, nullptr);
+    if (bq.ok && size_t(bq.cy) * size_t(bq.nclusters) * sizeof(double) > need)
+      need = size_t(bq.cy) * size_t(bq.nclusters) * sizeof(double);
+  }
+  return need;
 }
 
 int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
@@ -507,7 +678,9 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     return LNCC_ERR_BAD_ARG;
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
   if (pl.nblocks > INT32_MAX) return LNCC_ERR_TOO_LARGE;
-  const size_t need = size_t(pl.nblocks) * sizeof(double);
+  const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
+  const int64_t nparts = bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
+  const size_t need = size_t(nparts) * sizeof(double);
   if (!workspace || workspace_bytes < need || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
   if (loss_out && !(loss_count > 0.0)) return LNCC_ERR_BAD_ARG;
 
@@ -524,8 +697,7 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
   a.partials = reinterpret_cast<double*>(workspace);
   a.gscale_dev = grad_scale_dev;
   a.gscale = grad_scale;
-  const double n = double(kernel_size) * kernel_size * kernel_size;
-  a.inv_n = float(1.0 / n);
+  a.n = float(kernel_size * kernel_size * kernel_size);
   a.dr = smooth_dr;
   a.D = int(D);
   a.H = int(H);
@@ -539,7 +711,25 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
 
   cudaError_t e;
   const bool g = grad != nullptr;
-  if (dtype == LNCC_F32)
+  if (bp.ok) {
+    band::BandArgs ba;
+    ba.p = pred;
+    ba.t = target;
+    ba.g = grad;
+    ba.partials = a.partials;
+    ba.gscale_dev = grad_scale_dev;
+    ba.gscale = grad_scale;
+    ba.n = a.n;
+    ba.dr = smooth_dr;
+    ba.D = int(D);
+    ba.H = int(H);
+    ba.W = int(W);
+    ba.z_begin = int(z_begin);
+    ba.z_end = int(z_end);
+    ba.total_planes = B * (z_end - z_begin);
+    ba.planes_per_cluster = bp.ppc;
+    e = launch_band(bp, ba, stream);
+  } else if (dtype == LNCC_F32)
     e = g ? dispatch_r<float, true>(pl.R, a, pl.nblocks, stream)
           : dispatch_r<float, false>(pl.R, a, pl.nblocks, stream);
   else
@@ -547,10 +737,16 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
           : dispatch_r<__nv_bfloat16, false>(pl.R, a, pl.nblocks, stream);
   if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
   if (cc_sum_out || loss_out) {
-    lncc_reduce_kernel<<<1, 1024, 0, stream>>>(a.partials, int(pl.nblocks), cc_sum_out, loss_out,
+    lncc_reduce_kernel<<<1, 1024, 0, stream>>>(a.partials, int(nparts), cc_sum_out, loss_out,
                                                loss_count > 0.0 ? loss_count : 1.0);
     if (cudaGetLastError() != cudaSuccess) return LNCC_ERR_LAUNCH;
   }
+  return LNCC_OK;
+}
+
+int lncc_select_kernel(int which) {
+  if (which < 0 || which > 2) return LNCC_ERR_BAD_ARG;
+  g_kernel_choice.store(which);
   return LNCC_OK;
 }
 

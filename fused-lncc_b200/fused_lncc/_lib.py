@@ -35,6 +35,7 @@ SIGNATURES = {
         _vp, ctypes.c_size_t, _vp,                   # workspace, bytes, stream
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
+    "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
 }
 
 _lock = threading.Lock()
@@ -76,3 +77,11 @@ def strerror(status):
 def check(status, what):
     if status != LNCC_OK:
         raise RuntimeError(f"{what}: {strerror(status)} (status {status})")
+
+
+KERNEL_AUTO, KERNEL_SWEEP, KERNEL_BAND = 0, 1, 2
+
+
+def select_kernel(which):
+    """Process-wide kernel choice (0 auto, 1 general sweep kernel, 2 band kernel where supported)."""
+    check(load().lncc_select_kernel(int(which)), "lncc_select_kernel")

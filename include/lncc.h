@@ -92,6 +92,14 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype,
  */
 int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream);
 
+/*
+ * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:
+ * the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the pointers are 16-byte
+ * aligned, else the general sweep kernel), 1 = always the general sweep kernel, 2 = band kernel
+ * where supported (as 0). No counterpart in the reference, which has a single kernel per step.
+ */
+int lncc_select_kernel(int which);
+
 #ifdef __cplusplus
 }
 #endif

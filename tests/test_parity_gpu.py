@@ -128,30 +128,47 @@ def test_regression_28cube(k):
     assert_fp32_parity(p, t, k)
 
 
-@pytest.mark.parametrize("name,p,t", [
-    ("zeros", torch.zeros(2, 2, 32, 32, 32), torch.zeros(2, 2, 32, 32, 32)),
-    ("const5", torch.full((2, 2, 32, 32, 32), 5.0), torch.full((2, 2, 32, 32, 32), 5.0)),
-    ("const1e4", torch.full((1, 1, 32, 32, 32), 1e4), torch.full((1, 1, 32, 32, 32), 1e4)),
+@pytest.mark.parametrize("name,p,t,exact", [
+    ("zeros", torch.zeros(2, 2, 32, 32, 32), torch.zeros(2, 2, 32, 32, 32), True),
+    ("const5", torch.full((2, 2, 32, 32, 32), 5.0), torch.full((2, 2, 32, 32, 32), 5.0), True),
+    ("const1e4", torch.full((1, 1, 32, 32, 32), 1e4), torch.full((1, 1, 32, 32, 32), 1e4), False),
     ("near_const", torch.full((1, 2, 24, 24, 24), 3.0) + 1e-3 * torch.randn(1, 2, 24, 24, 24,
                                                                              generator=torch.Generator().manual_seed(5)),
-     torch.full((1, 2, 24, 24, 24), 3.0)),
+     torch.full((1, 2, 24, 24, 24), 3.0), False),
 ])
-def test_degenerate_inputs(name, p, t):
+def test_degenerate_inputs(name, p, t, exact):
+    """reference tests/test_robust.py:23-34: finite, in [0, 1.0001], finite grad. For small-integer
+    constants the window sums are exact in fp32, so the loss must also equal the fp64 oracle (and
+    an all-zero input must give an all-zero gradient). The gradient of a constant input is a
+    difference of nearly equal terms of size ~25*m*(n-m) (border windows have cc = 1 - O(dr)), which
+    no fp32 kernel, the reference's included, resolves; for 1e4 constants and near-constant windows
+    even the loss is below fp32 resolution. There only the reference's own assertions apply."""
     p, t = p.cuda(), t.cuda()
     lf, gf = fused(p, t, 7)
     assert np.isfinite(lf) and 0.0 <= lf <= 1.0001, (name, lf)
     assert torch.isfinite(gf).all(), name
-    lo, _ = oracle(p, t, 7)
-    assert abs(lf - lo) < 1e-3, (name, lf, lo)
+    if exact:
+        lo, go = oracle(p, t, 7)
+        assert abs(lf - lo) < FP32_LOSS_TOL, (name, lf, lo)
+        if go.abs().max() == 0:
+            assert gf.abs().max().item() == 0.0, name
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 2, 2, 2), (1, 1, 2, 40, 40), (1, 3, 7, 9, 11), (3, 5, 13, 17, 19),
                                    (1, 1, 128, 1, 1), (1, 1, 1, 1, 1), (2, 1, 1, 33, 65), (1, 1, 9, 1, 70)])
 @pytest.mark.parametrize("k", [3, 7, 9])
 def test_shape_edge_cases(shape, k):
+    """reference tests/test_robust.py:36-43 compares the loss only; the gradient is checked too,
+    except for a 1-voxel volume, where every window holds the same single voxel and the gradient is
+    a difference of two nearly equal terms (relative error ~ var/dr * eps in any fp32 kernel)."""
     g = torch.Generator().manual_seed(hash((shape, k)) % (2 ** 31))
     p = torch.randn(*shape, generator=g).cuda()
     t = torch.randn(*shape, generator=g).cuda()
+    if shape[2] * shape[3] * shape[4] == 1:
+        lf, gf = fused(p, t, k)
+        lo, _ = oracle(p, t, k)
+        assert abs(lf - lo) < FP32_LOSS_TOL and torch.isfinite(gf).all()
+        return
     assert_fp32_parity(p, t, k)
 
 
@@ -255,3 +272,50 @@ def test_plane_range_matches_whole_volume():
         parts += s_part.item()
         torch.testing.assert_close(g, g_full[:, :, z0:z1], rtol=1e-4, atol=1e-5)
     assert abs(parts - s_full.item()) < 1e-6 * max(1.0, abs(s_full.item()))
+
+
+# ---- both kernels: the cluster band kernel (default where it applies) and the general sweep ---------
+@pytest.fixture(params=["sweep", "band"])
+def kernel(request):
+    from fused_lncc import _lib
+    _lib.select_kernel(_lib.KERNEL_SWEEP if request.param == "sweep" else _lib.KERNEL_AUTO)
+    yield request.param
+    _lib.select_kernel(_lib.KERNEL_AUTO)
+
+
+@pytest.mark.parametrize("shape,k", [((2, 3, 20, 32, 64), 7), ((1, 2, 40, 48, 128), 9), ((2, 1, 9, 16, 8), 3),
+                                     ((1, 1, 33, 130, 16), 5), ((3, 1, 70, 17, 20), 7), ((1, 1, 6, 256, 16), 3)])
+def test_both_kernels_match_oracle(kernel, shape, k):
+    g = torch.Generator().manual_seed(sum(shape) * 31 + k)
+    p = torch.randn(*shape, generator=g).cuda()
+    t = torch.randn(*shape, generator=g).cuda()
+    assert_fp32_parity(p, t, k)
+
+
+@pytest.mark.parametrize("k", [3, 5, 7, 9])
+def test_band_equals_sweep_blurred(k):
+    from fused_lncc import _lib, synth
+    pred, target = synth.blurred_pair((2, 2, 48, 64, 128), device="cuda")
+    outs = []
+    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_AUTO):
+        _lib.select_kernel(which)
+        try:
+            outs.append(fused(pred, target, k))
+        finally:
+            _lib.select_kernel(_lib.KERNEL_AUTO)
+    (l1, g1), (l2, g2) = outs
+    assert abs(l1 - l2) < 1e-6
+    cos, rel = cos_rel(g2, g1)
+    assert cos > 0.999999 and rel < 1e-4, (cos, rel)
+
+
+def test_band_bf16_and_loss_only():
+    from fused_lncc import synth
+    pred, target = synth.blurred_pair((2, 2, 40, 64, 64), device="cuda", dtype=torch.bfloat16)
+    lb, gb = fused(pred, target, 9)
+    lo, go = oracle(pred, target, 9)
+    assert abs(lb - lo) < BF16_LOSS_TOL
+    _, rel = cos_rel(gb, go)
+    assert gb.dtype == torch.bfloat16 and rel < BF16_REL
+    with torch.no_grad():
+        assert abs(fused_lncc_loss(pred, target, 9).item() - lb) < 1e-7
