@@ -620,6 +620,32 @@ static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cud
   return cudaLaunchKernelExC(&cfg, bp.fn, args);
 }
 
+// ------------------------------------------------------------------------------------------------
+// fixed scratch for callers that cannot allocate device memory (lncc_fused_forward_noalloc)
+// ------------------------------------------------------------------------------------------------
+// Room for this many fp64 partial sums (512 KiB); every GPU that loads the library holds it until
+// the process exits. Each call's kernels write every partial they later read, so nothing needs
+// clearing between calls; calls that overlap on the GPU share the array and race.
+constexpr int64_t kNoAllocMaxPartials = 65536;
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxPartials];
+
+// Device address of g_noalloc_partials on the current device, looked up once per device. In host
+// code the symbol is only a host-side stand-in, never a device address.
+static int noalloc_scratch(double** out) {
+  static std::mutex mu;
+  static double* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LNCC_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_partials) != cudaSuccess || p == nullptr) return LNCC_ERR_CUDA;
+    addr[dev] = static_cast<double*>(p);
+  }
+  *out = addr[dev];
+  return LNCC_OK;
+}
+
 }  // namespace lncc
 
 using namespace lncc;
@@ -742,6 +768,22 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     if (cudaGetLastError() != cudaSuccess) return LNCC_ERR_LAUNCH;
   }
   return LNCC_OK;
+}
+
+int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype, int64_t B, int64_t D,
+                               int64_t H, int64_t W, int kernel_size, float smooth_dr, int64_t z_begin,
+                               int64_t z_end, void* grad, float grad_scale, const float* grad_scale_dev,
+                               double* cc_sum_out, float* loss_out, double loss_count, cudaStream_t stream) {
+  const size_t cap = size_t(kNoAllocMaxPartials) * sizeof(double);
+  const size_t need = lncc_workspace_bytes(B, D, H, W, kernel_size, dtype, z_begin, z_end);
+  if (need > cap) return LNCC_ERR_TOO_LARGE;
+  double* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != LNCC_OK) return st;
+  // need == 0 means invalid arguments: the regular entry point reports the precise status
+  return lncc_fused_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, z_begin, z_end, grad,
+                            grad_scale, grad_scale_dev, cc_sum_out, loss_out, loss_count, scratch, cap,
+                            stream);
 }
 
 int lncc_select_kernel(int which) {

@@ -36,6 +36,15 @@ SIGNATURES = {
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "lncc_fused_forward_noalloc": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int,                      # pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float,                # kernel_size, smooth_dr
+        _c_i64, _c_i64,                              # z_begin, z_end
+        _vp, ctypes.c_float, _vp,                    # grad, grad_scale, grad_scale_dev
+        _vp, _vp, ctypes.c_double,                   # cc_sum_out, loss_out, loss_count
+        _vp,                                         # stream
+    ]),
 }
 
 _lock = threading.Lock()

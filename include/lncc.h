@@ -93,6 +93,27 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype,
 int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream);
 
 /*
+ * lncc_fused_forward without a caller-provided workspace. No counterpart in the reference. It is
+ * for callers that cannot call cudaMalloc, for example code running where the allocator is owned by
+ * someone else (a framework's caching allocator or a pool that must not grow), or where allocating
+ * is forbidden at that point (inside a tight real-time loop). The scratch that lncc_fused_forward
+ * takes as `workspace` here is a fixed array in the library's device memory: 65536 fp64 partial sums
+ * (512 KiB) per GPU, held until the process exits. Sizes that need more than that return
+ * LNCC_ERR_TOO_LARGE; lncc_workspace_bytes() tells how much a call needs. Nothing is allocated: the
+ * first call on each device only looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current, so make that first call before capturing a stream into a CUDA graph. All
+ * calls share the one array: calls that overlap on the GPU (different streams, no ordering) race.
+ * Every other argument means exactly what it means for lncc_fused_forward.
+ */
+int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype,
+                               int64_t B, int64_t D, int64_t H, int64_t W,
+                               int kernel_size, float smooth_dr,
+                               int64_t z_begin, int64_t z_end,
+                               void* grad, float grad_scale, const float* grad_scale_dev,
+                               double* cc_sum_out, float* loss_out, double loss_count,
+                               cudaStream_t stream);
+
+/*
  * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:
  * the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the pointers are 16-byte
  * aligned, else the general sweep kernel), 1 = always the general sweep kernel, 2 = band kernel
