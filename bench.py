@@ -30,13 +30,27 @@ for _p in (PKG, ROOT):
 import torch  # noqa: E402
 
 WORKLOADS = {
-    # name: (shape, k, dtype, construction)
-    "headline": ((2, 16, 128, 128, 128), 7, "fp32", "blurred"),
-    "config1": ((1, 1, 64, 64, 64), 7, "fp32", "blurred"),
-    "mri": ((8, 1, 160, 192, 224), 9, "bf16", "mri"),
-    "small": ((2, 4, 128, 128, 128), 7, "fp32", "blurred"),   # profiling-sized case of headline
+    # name: (shape, k, dtype, construction); configs of BASELINE.json
+    "headline": ((2, 16, 128, 128, 128), 7, "fp32", "blurred"),        # config 2, N*C volumes sharded
+    "config1": ((1, 1, 64, 64, 64), 7, "fp32", "blurred"),             # config 1
+    "mri": ((8, 1, 160, 192, 224), 9, "bf16", "mri"),                  # config 3, volumes sharded
+    "ksweep3": ((1, 1, 256, 256, 256), 3, "fp32", "blurred"),          # config 4, D-slabs
+    "ksweep5": ((1, 1, 256, 256, 256), 5, "fp32", "blurred"),
+    "ksweep7": ((1, 1, 256, 256, 256), 7, "fp32", "blurred"),
+    "ksweep9": ((1, 1, 256, 256, 256), 9, "fp32", "blurred"),
+    "gigavoxel": ((1, 1, 1024, 1024, 1024), 7, "fp32", "gigavoxel"),  # config 5, D-slabs
+    "small": ((2, 4, 128, 128, 128), 7, "fp32", "blurred"),            # profiling-sized headline case
 }
+SLAB_WORKLOADS = {"ksweep3", "ksweep5", "ksweep7", "ksweep9", "gigavoxel"}
 METRIC = "fwd+bwd Gvoxel/s at (2,16,128^3) fp32 k=7"
+
+
+def metric_name(workload):
+    """The headline metric string for the headline workload, the same unit for the others."""
+    if workload == "headline":
+        return METRIC
+    shape, k, dtype, _ = WORKLOADS[workload]
+    return f"fwd+bwd Gvoxel/s at ({','.join(map(str, shape))}) {dtype} k={k}"
 BYTES_PER_VOXEL = {"fp32": 12, "bf16": 6}   # read pred + read target + write grad
 
 
@@ -128,6 +142,8 @@ def make_inputs(workload, device):
     tdt = torch.float32 if dtype == "fp32" else torch.bfloat16
     if kind == "blurred":
         pred, target = synth.blurred_pair(shape, device=device, dtype=tdt)
+    elif kind == "gigavoxel":
+        pred, target = synth.gigavoxel_pair(shape, device=device, dtype=tdt)
     else:
         pred, target = synth.mri_pair(shape, device=device, dtype=tdt)
     return pred, target, k, dtype
@@ -186,7 +202,7 @@ def run_reference(args, rank, world):
                                        sample_volumes=args.cpu_sample_volumes)
     shape = WORKLOADS[args.workload][0]
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gvoxel/s", "n_gpus": world,
+        "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
         "steps": steps, "warmup": max(1, min(args.warmup, 1)),
         "ms_per_step": info["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -235,24 +251,44 @@ def main():
     shape = WORKLOADS[args.workload][0]
     n, c = shape[:2]
     nvol = n * c
-    b0, b1 = volume_range(nvol, world, rank)
-    vshape = (nvol, 1, *shape[2:])
-    p_loc = pred.reshape(vshape)[b0:b1].contiguous().requires_grad_(True)
-    t_loc = target.reshape(vshape)[b0:b1].contiguous()
+    slabs = args.workload in SLAB_WORKLOADS
     input_sha = None
     if rank == 0 and args.workload == "config1":
         input_sha = fused_lncc.synth.sha256_of(pred)
+    m_global = float(nvol) * shape[2] * shape[3] * shape[4]
+    if slabs:
+        # one volume split into D-slabs; each rank keeps its owned planes plus 2r halo planes
+        from fused_lncc.dist import SlabPlan, slab_lncc_loss
+        plan = SlabPlan(shape[2], world, rank, k)
+        lo, e = plan.own_range
+        p_loc = torch.zeros((1, plan.depth, shape[3], shape[4]), dtype=pred.dtype, device=dev)
+        t_loc = torch.zeros_like(p_loc)
+        p_loc[:, lo:e] = pred.reshape(shape[2:])[None, plan.z0:plan.z1]
+        t_loc[:, lo:e] = target.reshape(shape[2:])[None, plan.z0:plan.z1]
+        p_loc.requires_grad_(True)
+        b0, b1 = 0, 1
+        z_rng = (lo, e)
+        vox_local = plan.own * shape[3] * shape[4]
+        parallelism = f"D-slabs/{world} (2r halo planes exchanged per side)"
+
+        def loss_fn(p, t):
+            return slab_lncc_loss(p, t, plan, k)
+    else:
+        b0, b1 = volume_range(nvol, world, rank)
+        vshape = (nvol, 1, *shape[2:])
+        p_loc = pred.reshape(vshape)[b0:b1].contiguous().requires_grad_(True)
+        t_loc = target.reshape(vshape)[b0:b1].contiguous()
+        z_rng = (0, shape[2])
+        vox_local = p_loc.numel()
+        parallelism = f"volumes/{world}"
+        if world > 1:
+            def loss_fn(p, t):
+                return sharded_lncc_loss(p, t, k, m_global=m_global)
+        else:
+            def loss_fn(p, t):
+                return fused_lncc.fused_lncc_loss(p, t, k)
     del pred, target
     torch.cuda.empty_cache()
-    m_global = float(nvol) * shape[2] * shape[3] * shape[4]
-    vox_local = p_loc.numel()
-
-    if world > 1:
-        def loss_fn(p, t):
-            return sharded_lncc_loss(p, t, k, m_global=m_global)
-    else:
-        def loss_fn(p, t):
-            return fused_lncc.fused_lncc_loss(p, t, k)
 
     def step():
         p_loc.grad = None
@@ -276,14 +312,18 @@ def main():
     sampler = ClockSampler(local_rank)
     lib = _lib.load()
     esz = 4 if dtype == "fp32" else 2
-    nb, D, H, W = p_loc.shape[0], shape[2], shape[3], shape[4]
-    ws_bytes = lib.lncc_workspace_bytes(nb, D, H, W, k, 0 if dtype == "fp32" else 1, 0, D)
+    dtc = 0 if dtype == "fp32" else 1
+    if slabs:
+        nb, D, H, W = 1, p_loc.shape[1], shape[3], shape[4]
+    else:
+        nb, D, H, W = p_loc.shape[0], shape[2], shape[3], shape[4]
+    ws_bytes = lib.lncc_workspace_bytes(nb, D, H, W, k, dtc, z_rng[0], z_rng[1])
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    gbuf = torch.empty_like(p_loc)
+    gbuf = torch.empty((nb, z_rng[1] - z_rng[0], H, W), dtype=p_loc.dtype, device=dev)
 
     def kernel_launch():
-        st = lib.lncc_fused_forward(p_loc.data_ptr(), t_loc.data_ptr(), 0 if dtype == "fp32" else 1,
-                                    nb, D, H, W, k, 1e-5, 0, D, gbuf.data_ptr(), -1.0 / m_global, None,
+        st = lib.lncc_fused_forward(p_loc.data_ptr(), t_loc.data_ptr(), dtc, nb, D, H, W, k, 1e-5,
+                                    z_rng[0], z_rng[1], gbuf.data_ptr(), -1.0 / m_global, None,
                                     None, None, 1.0, ws.data_ptr(), ws_bytes, stream.cuda_stream)
         _lib.check(st, "bench launch")
 
@@ -338,16 +378,18 @@ def main():
         return 0
 
     # ---- e2e: public call with host buffers ---------------------------------------------------------
-    p_host = p_loc.detach().cpu().pin_memory()
-    t_host = t_loc.cpu().pin_memory()
-    p_dev = torch.empty_like(p_loc).requires_grad_(True)
-    t_dev = torch.empty_like(t_loc)
+    # host copies of this rank's own voxels only (slab halos arrive over NCCL inside the step)
+    own = (slice(None), slice(z_rng[0], z_rng[1])) if slabs else (slice(None),)
+    p_host = p_loc.detach()[own].cpu().pin_memory()
+    t_host = t_loc[own].cpu().pin_memory()
+    p_dev = torch.zeros_like(p_loc).requires_grad_(True)
+    t_dev = torch.zeros_like(t_loc)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
     def e2e_step():
         with torch.no_grad():
-            p_dev.copy_(p_host, non_blocking=True)
-            t_dev.copy_(t_host, non_blocking=True)
+            p_dev[own].copy_(p_host, non_blocking=True)
+            t_dev[own].copy_(t_host, non_blocking=True)
         p_dev.grad = None
         loss = loss_fn(p_dev, t_dev)
         loss.backward()
@@ -384,21 +426,24 @@ def main():
         achieved = vox_local * bpv / (result["ms_kernel"] * 1e-3) / 1e9   # GB/s, rank 0's launch
         traffic = profile_traffic("lncc_sweep_kernel", args.workload if world == 1 else None)
         line = {
-            "metric": METRIC, "value": value, "unit": "Gvoxel/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": result["ms_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "shape": list(shape), "kernel_size": k,
                        "input_dtype": dtype, "volumes_per_rank": b1 - b0,
-                       "parallelism": f"volumes/{world}", "l2": "flushed (256 MiB write) before every step",
+                       "parallelism": parallelism, "l2": "flushed (256 MiB write) before every step",
                        "input_sha256": input_sha},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
                          "traffic": traffic, "kernel": "lncc_sweep_kernel",
                          "algorithmic_bytes_per_voxel": bpv, "ms_per_launch": result["ms_kernel"]},
             "e2e": {"value": vox_global / (ms_e2e * 1e-3) / 1e9, "unit": "Gvoxel/s",
-                    "h2d_bytes_per_step": 2 * vox_local * esz, "d2h_bytes_per_step": 4,
+                    "h2d_bytes_per_step": 2 * p_host.numel() * esz, "d2h_bytes_per_step": 4,
                     "ms_per_step": ms_e2e},
-            "gpu_launches": 3 * args.steps,
+            # fused kernel + loss reduction per compute call (3 calls per slab step when halos are
+            # exchanged, to overlap the interior), plus the grad_out scale kernel
+            "gpu_launches": (2 * (3 if slabs and world > 1 else 1) + 1) * args.steps,
             "clocks": clocks,
             "loss": loss_val,
         }

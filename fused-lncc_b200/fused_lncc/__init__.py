@@ -38,7 +38,8 @@ def _check_pair(pred, target):
 
 
 def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_scale=None,
-               loss_count=None, z_range=None, cc_sum_out=None, loss_out=None, grad_scale_dev=None):
+               loss_count=None, z_range=None, cc_sum_out=None, loss_out=None, grad_scale_dev=None,
+               out=None):
     """Run the fused kernel once: returns (loss, grad).
 
     pred/target: contiguous (..., D, H, W) CUDA tensors, fp32 or bf16; the leading dims are
@@ -48,6 +49,7 @@ def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_s
     z_range: (z_begin, z_end) output planes of every volume (default the whole volume); planes of
              the array outside the range act as halo. grad then has z_end - z_begin planes.
     cc_sum_out / loss_out: optional preallocated fp64 / fp32 one-element CUDA tensors.
+    out: optional preallocated contiguous gradient tensor of the grad's shape and pred's dtype.
     Returns (loss: 0-dim fp32 tensor, grad: tensor or None).
     """
     _check_pair(pred, target)
@@ -68,7 +70,14 @@ def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_s
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         g = None
         if grad:
-            g = torch.empty((*lead, z1 - z0, H, W), dtype=pred.dtype, device=dev)
+            shape = (*lead, z1 - z0, H, W)
+            if out is not None:
+                if (tuple(out.shape) != shape or out.dtype != pred.dtype or out.device != dev
+                        or not out.is_contiguous()):
+                    raise RuntimeError(f"fused_lncc: out must be a contiguous {shape} {pred.dtype} tensor")
+                g = out
+            else:
+                g = torch.empty(shape, dtype=pred.dtype, device=dev)
         if loss_out is None:
             loss_out = torch.empty((), dtype=torch.float32, device=dev)
         if grad_scale is None:
