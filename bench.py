@@ -424,7 +424,9 @@ def main():
         peak, peak_src = measured_peak_gbs()
         bpv = BYTES_PER_VOXEL[dtype]
         achieved = vox_local * bpv / (result["ms_kernel"] * 1e-3) / 1e9   # GB/s, rank 0's launch
-        traffic = profile_traffic("lncc_sweep_kernel", args.workload if world == 1 else None)
+        # which kernel the library picks for this shape (the band kernel's conditions, include/lncc.h)
+        kname = ("lncc_band_kernel" if (W <= 128 and W % 4 == 0 and H <= 256) else "lncc_sweep_kernel")
+        traffic = profile_traffic(kname, args.workload) if world == 1 else None
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
             "steps": args.steps,
@@ -436,7 +438,7 @@ def main():
                        "input_sha256": input_sha},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
-                         "traffic": traffic, "kernel": "lncc_sweep_kernel",
+                         "traffic": traffic, "kernel": kname,
                          "algorithmic_bytes_per_voxel": bpv, "ms_per_launch": result["ms_kernel"]},
             "e2e": {"value": vox_global / (ms_e2e * 1e-3) / 1e9, "unit": "Gvoxel/s",
                     "h2d_bytes_per_step": 2 * p_host.numel() * esz, "d2h_bytes_per_step": 4,
