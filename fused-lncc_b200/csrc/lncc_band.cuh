@@ -22,8 +22,9 @@
 // Steps are software-pipelined with ONE split cluster barrier per step c:
 //   A(c) -> arrive | prefetch, D(c-2) | wait -> B(c), C(c-1) -> __syncthreads
 // DW and ADJ are double-buffered by step parity, so a buffer is rewritten only two steps after its
-// remote readers have passed a barrier. Global loads are issued after the arrive (a release fence)
-// so that it never waits for them.
+// remote readers have passed a barrier. Only the warps that pushed rows into a neighbour arrive with
+// a cluster-scope release; the others fence at CTA scope and arrive relaxed. Global loads are issued
+// after the arrive so that no fence waits for them.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -100,6 +101,13 @@ __device__ __forceinline__ void cluster_arrive() {
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive for a warp that wrote no other CTA's shared memory since its last arrive: a CTA-scope fence
+// orders its local shared-memory writes, and the arrive itself is relaxed. A cluster-scope release
+// (cluster_arrive) waits for every outstanding store and is the dominant cost of a plane step.
+__device__ __forceinline__ void cluster_arrive_local() {
+  asm volatile("fence.acq_rel.cta;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 
 // ---- TMEM (tensor memory) used as a per-thread ring buffer ----------------------------------------
@@ -233,6 +241,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
   const bool cl_thread = tid < NCL;
   const int cl_r0 = cl_seg * L;
   const bool cl_in_col = cl_thread && cl_col < W;
+  // Warps that push rows into a neighbour CTA (DW in A, ADJ in B) arrive with cluster-scope release
+  // semantics; the others only need CTA scope. The condition is uniform across each warp.
+  const bool pushes_remote = (warp < R) || (warp >= TH - R) ||
+                             (cl_thread && (cl_r0 < R || cl_r0 + L > TH - R));
 
   float gs = 0.f;
   if (GRAD) gs = 2.f * a.gscale * (a.gscale_dev ? __ldg(a.gscale_dev) : 1.f);
@@ -415,8 +427,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
             *reinterpret_cast<float4*>(&dn->DW[buf][f][warp - (TH - R)][x_rl]) = w4;
         }
       }
-      // release covers the DW stores; global loads are issued after it so the fence never waits on them
-      cluster_arrive();
+      // release covers the DW pushes (and the ADJ pushes of the previous B); global loads are issued
+      // after it so that the fence never waits on them
+      if (pushes_remote) cluster_arrive();
+      else cluster_arrive_local();
       pn = tn = po = to = zero4;
       if (c + 1 < c_end) {
         if (raw_ok(c + 1 + R)) {
