@@ -22,7 +22,9 @@
 // Steps are software-pipelined with ONE split cluster barrier per step c:
 //   A(c) -> arrive | prefetch, D(c-2) | wait -> B(c), C(c-1) -> __syncthreads
 // DW and ADJ are double-buffered by step parity, so a buffer is rewritten only two steps after its
-// remote readers have passed a barrier. Only the warps that pushed rows into a neighbour arrive with
+// remote readers have passed a barrier. AH is double-buffered too where shared memory allows (r <= 3):
+// D(c-2) reads it between arrive and wait while C(c-1) writes it after the wait. With one AH buffer
+// (r = 4) a CTA barrier after the wait keeps C(c-1) behind every D(c-2) of the CTA. Only the warps that pushed rows into a neighbour arrive with
 // a cluster-scope release; the others fence at CTA scope and arrive relaxed. Global loads are issued
 // after the arrive so that no fence waits for them.
 #pragma once
@@ -57,11 +59,14 @@ struct BandArgs {
 // DW and ADJ hold the CTA's own rows at [R, R+TH) plus R halo rows on each side: rows [0, R) are
 // pushed by the CTA above (its last R rows), rows [R+TH, TH+2R) by the CTA below. Halo rows with no
 // neighbour stay zero (the volume's zero padding).
+// AH buffers: two where they fit in the 227 KB a CTA may use
+template <int R>
+constexpr int AH_BUFS = R <= 3 ? 2 : 1;
 template <int R>
 struct Smem {
   float DW[2][5][TH + 2 * R][WMAX];
   float ADJ[2][3][TH + 2 * R][WMAX];
-  float AH[3][TH][WMAX];
+  float AH[AH_BUFS<R>][3][TH][WMAX];
   double red[NT / 32];
   uint32_t tmem_base;
 };
@@ -69,7 +74,10 @@ struct Smem {
 // may allocate all 512 TMEM columns without waiting for another CTA.
 template <int R>
 constexpr int smem_bytes() { return int((sizeof(Smem<R>) + 1023) / 1024 * 1024); }
-static_assert(smem_bytes<1>() > 116 * 1024 && smem_bytes<4>() <= 227 * 1024, "band smem");
+static_assert(smem_bytes<1>() > 116 * 1024, "band smem: one CTA per SM");
+static_assert(smem_bytes<1>() <= 227 * 1024 && smem_bytes<2>() <= 227 * 1024 && smem_bytes<3>() <= 227 * 1024 &&
+                  smem_bytes<4>() <= 227 * 1024,
+              "band smem: 227 KB per CTA");
 
 template <typename S>
 struct Vec4;
@@ -298,6 +306,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
     // D [RL]: W box of AH, D running sum through the TMEM ring, gradient of output plane c-R
     auto phase_D = [&](int c, float4 pcv, float4 tcv) {
       const int it = c - c0;
+      const int ahb = AH_BUFS<R> == 2 ? (it & 1) : 0;  // C(c) wrote AH[(c - c0) & 1]
       const uint32_t ta = tmem + uint32_t(12 * (it % K));
       uint32_t u[12];
       const bool has_old = it >= K;
@@ -306,7 +315,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
       float v[12];
 #pragma unroll
       for (int f = 0; f < 3; ++f) {
-        const float4 w4 = wbox<R>(*reinterpret_cast<const float4*>(&sm.AH[f][warp][x_rl]), lane);
+        const float4 w4 = wbox<R>(*reinterpret_cast<const float4*>(&sm.AH[ahb][f][warp][x_rl]), lane);
         v[4 * f + 0] = w4.x; v[4 * f + 1] = w4.y; v[4 * f + 2] = w4.z; v[4 * f + 3] = w4.w;
       }
       if (has_old) {
@@ -386,6 +395,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
     // C [CL]: H box of ADJ[buf] (halo rows from neighbours) -> AH
     auto phase_C = [&](int c, int buf) {
       (void)c;
+      const int ahb = AH_BUFS<R> == 2 ? buf : 0;  // buf = (c - c0) & 1
       float s[3] = {0.f, 0.f, 0.f};
       float win[3][2 * R + 1];
       const float* adp = &sm.ADJ[buf][0][cl_r0][cl_col];
@@ -404,14 +414,14 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
         if (q >= 2 * R) {
           const int r = cl_r0 + q - 2 * R;
 #pragma unroll
-          for (int f = 0; f < 3; ++f) sm.AH[f][r][cl_col] = s[f];
+          for (int f = 0; f < 3; ++f) sm.AH[ahb][f][r][cl_col] = s[f];
         }
       }
     };
 
     // Software pipeline, one cluster barrier per step:
     //   step c:  A(c) -> arrive | prefetch, D(c-2) | wait -> B(c), C(c-1) -> __syncthreads
-    // DW and ADJ are double-buffered by step parity, AH is local.
+    // DW and ADJ are double-buffered by step parity, AH (local) too when AH_BUFS<R> == 2.
     for (int c = c0; c <= c_end + 1; ++c) {
       const int buf = (c - c0) & 1;
       if (c < c_end) {
@@ -454,6 +464,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_band_kernel(const BandArgs a) {
       pc = pcn;
       tc = tcn;
       cluster_wait();
+      if (AH_BUFS<R> == 1) __syncthreads();  // every D(c-2) of the CTA has read AH
       if (cl_thread) {
         if (c < c_end) phase_B(c, buf);
         if (GRAD && c - 1 >= c0 && c - 1 < c_end) phase_C(c - 1, buf ^ 1);
