@@ -35,6 +35,7 @@
 #define LNCC_VERSION_NUM 100  // 0.1.0
 
 #include "lncc_band.cuh"
+#include "lncc_compat.cuh"
 
 namespace lncc {
 
@@ -646,6 +647,38 @@ static int noalloc_scratch(double** out) {
   return LNCC_OK;
 }
 
+// ---- materialising compat kernels (lncc_compat.cuh) ---------------------------------------------
+template <int MODE, typename S>
+static cudaError_t launch_compat(int R, const compat::Args& a, int64_t nblocks, cudaStream_t st) {
+  const dim3 grid{unsigned(nblocks)}, block{unsigned(compat::NT)};
+  switch (R) {
+    case 1: compat::compat_kernel<1, MODE, S><<<grid, block, 0, st>>>(a); break;
+    case 2: compat::compat_kernel<2, MODE, S><<<grid, block, 0, st>>>(a); break;
+    case 3: compat::compat_kernel<3, MODE, S><<<grid, block, 0, st>>>(a); break;
+    case 4: compat::compat_kernel<4, MODE, S><<<grid, block, 0, st>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// Geometry and size checks shared by the three compat entry points; fills the tiling fields of `a`.
+static int compat_plan(int64_t B, int64_t D, int64_t H, int64_t W, int k, compat::Args* a, int64_t* nblocks) {
+  if (!valid_k(k)) return LNCC_ERR_KERNEL_SIZE;
+  if (B < 1 || D < 1 || H < 1 || W < 1) return LNCC_ERR_BAD_ARG;
+  if (D > INT32_MAX / 2 || H > INT32_MAX / 2 || W > INT32_MAX / 2) return LNCC_ERR_TOO_LARGE;
+  a->D = int(D);
+  a->H = int(H);
+  a->W = int(W);
+  a->tiles_x = int((W + compat::TW - 1) / compat::TW);
+  a->tiles_y = int((H + compat::TH - 1) / compat::TH);
+  a->chunks = int((D + compat::ZCHUNK - 1) / compat::ZCHUNK);
+  const int64_t nb = B * a->chunks * int64_t(a->tiles_y) * a->tiles_x;
+  if (nb > INT32_MAX) return LNCC_ERR_TOO_LARGE;
+  a->n = float(k * k * k);
+  *nblocks = nb;
+  return LNCC_OK;
+}
+
 }  // namespace lncc
 
 using namespace lncc;
@@ -790,6 +823,69 @@ int lncc_select_kernel(int which) {
   if (which < 0 || which > 2) return LNCC_ERR_BAD_ARG;
   g_kernel_choice.store(which);
   return LNCC_OK;
+}
+
+int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                      int64_t W, int kernel_size, float smooth_dr, float* ncc, float* A, float* Bc, float* Cc,
+                      cudaStream_t stream) {
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!pred || !target) return LNCC_ERR_BAD_ARG;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz)) return LNCC_ERR_BAD_ARG;
+  for (const float* m : {static_cast<const float*>(ncc), static_cast<const float*>(A),
+                         static_cast<const float*>(Bc), static_cast<const float*>(Cc)})
+    if (uintptr_t(m) % 4) return LNCC_ERR_BAD_ARG;
+  a.in[0] = pred;
+  a.in[1] = target;
+  a.out[0] = ncc;
+  a.out[1] = A;
+  a.out[2] = Bc;
+  a.out[3] = Cc;
+  a.ndr = a.n * smooth_dr;
+  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
+                                          : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+int lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const void* pred, const void* target,
+                       int dtype, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, float scale,
+                       void* grad, cudaStream_t stream) {
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!A || !Bc || !Cc || !pred || !target || !grad) return LNCC_ERR_BAD_ARG;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(grad) % esz)) return LNCC_ERR_BAD_ARG;
+  if ((uintptr_t(A) % 4) || (uintptr_t(Bc) % 4) || (uintptr_t(Cc) % 4)) return LNCC_ERR_BAD_ARG;
+  a.in[0] = A;
+  a.in[1] = Bc;
+  a.in[2] = Cc;
+  a.p = pred;
+  a.t = target;
+  a.out[0] = grad;
+  a.scale = scale;
+  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::BWD, float>(kernel_size / 2, a, nb, stream)
+                                          : launch_compat<compat::BWD, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size,
+               cudaStream_t stream) {
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!x || !y || (uintptr_t(x) % 4) || (uintptr_t(y) % 4)) return LNCC_ERR_BAD_ARG;
+  a.in[0] = x;
+  a.out[0] = y;
+  const cudaError_t e = launch_compat<compat::BOX, float>(kernel_size / 2, a, nb, stream);
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {

@@ -16,7 +16,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["fused_lncc_loss", "lncc_fused", "FusedLNCC"]
+__all__ = ["fused_lncc_loss", "lncc_fused", "FusedLNCC", "compat"]
 
 _DTYPES = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16}
 
@@ -178,3 +178,6 @@ def fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5):
     assert kernel_size % 2 == 1, "kernel_size must be odd"
     need_grad = bool(pred.requires_grad and torch.is_grad_enabled())
     return FusedLNCC.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr, need_grad)
+
+
+from . import compat  # noqa: E402  (registers the reference's fused_lncc::forward/backward ops)

@@ -45,6 +45,18 @@ SIGNATURES = {
         _vp, _vp, ctypes.c_double,                   # cc_sum_out, loss_out, loss_count
         _vp,                                         # stream
     ]),
+    "lncc_maps_forward": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int,                      # pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float,                # kernel_size, smooth_dr
+        _vp, _vp, _vp, _vp, _vp,                     # ncc, A, Bc, Cc, stream
+    ]),
+    "lncc_maps_backward": (ctypes.c_int, [
+        _vp, _vp, _vp, _vp, _vp, ctypes.c_int,       # A, Bc, Cc, pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float, _vp, _vp,      # kernel_size, scale, grad, stream
+    ]),
+    "lncc_box3d": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
 }
 
 _lock = threading.Lock()

@@ -114,6 +114,39 @@ int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype,
                                cudaStream_t stream);
 
 /*
+ * Materialising compat path: the reference extension's three entry points with their outputs, for
+ * debugging and for code written against them (the reference's own tests call them directly,
+ * tests/test_pytest.py:38-51, tests/verify_fwd.py:20-24). The fused entry point above is the
+ * training path; these write full fp32 maps (16 B/voxel for the forward).
+ *
+ * lncc_maps_forward replaces fused_lncc_cuda.lncc_forward (lncc3d.cu:127-161): from (B, D, H, W)
+ * pred/target of `dtype` it writes four fp32 (B, D, H, W) maps: ncc (cc clamped to 1, NaN kept) and
+ * the adjoints A = dncc/dSp, Bc = dncc/dvar_p, Cc = dncc/dcross of lncc3d.cu:100-107 (zero where
+ * cc >= 1 or NaN). Any of ncc/A/Bc/Cc may be NULL to skip that map.
+ */
+int lncc_maps_forward(const void* pred, const void* target, int dtype,
+                      int64_t B, int64_t D, int64_t H, int64_t W,
+                      int kernel_size, float smooth_dr,
+                      float* ncc, float* A, float* Bc, float* Cc, cudaStream_t stream);
+
+/*
+ * Replaces fused_lncc_cuda.lncc_backward (lncc3d.cu:253-284): writes
+ * grad = scale * (box(A) + 2*pred*box(Bc) + target*box(Cc)) in `dtype` (pred's), for fp32 maps A, Bc,
+ * Cc and pred/target of `dtype`, all (B, D, H, W).
+ */
+int lncc_maps_backward(const float* A, const float* Bc, const float* Cc,
+                       const void* pred, const void* target, int dtype,
+                       int64_t B, int64_t D, int64_t H, int64_t W,
+                       int kernel_size, float scale, void* grad, cudaStream_t stream);
+
+/*
+ * Replaces fused_lncc_cuda.box3d_sep_forward (lncc3d.cu:329-344): y = zero-padded k^3 box sum of the
+ * fp32 (B, D, H, W) array x. y must not overlap x.
+ */
+int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size,
+               cudaStream_t stream);
+
+/*
  * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:
  * the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the pointers are 16-byte
  * aligned, else the general sweep kernel), 1 = always the general sweep kernel, 2 = band kernel

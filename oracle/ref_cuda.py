@@ -21,8 +21,10 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 NAME = "fused_lncc_cuda"
-# where the reference checkout lies on the build machine; the GPU box only has the built module
-REF_ROOT = os.environ.get("LNCC_REFERENCE_ROOT", "/root/reference")
+# the reference checkout on the build machine (default: a directory "reference" beside this
+# repository); the GPU machines only get the built module
+REF_ROOT = os.environ.get("LNCC_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 REF_SRC = os.path.join(REF_ROOT, "fused_lncc", "csrc", "lncc3d.cu")
 
 

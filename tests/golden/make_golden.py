@@ -60,7 +60,9 @@ def sha(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("LNCC_REFERENCE_ROOT", "/root/reference"))
+    # default: a checkout named "reference" beside this repository
+    sibling = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference")
+    ap.add_argument("--reference", default=os.environ.get("LNCC_REFERENCE_ROOT", sibling))
     args = ap.parse_args()
     ref = load_reference(args.reference)
     torch.set_num_threads(os.cpu_count() or 1)

@@ -52,3 +52,32 @@ def test_fake_impls_give_fp32_loss_and_pred_dtype_grad():
         loss, g = torch.ops.fused_lncc.fwd_grad(p, p, 7, 1e-5, True)
         assert loss.dtype == torch.float32 and loss.dim() == 0
         assert g.dtype == torch.bfloat16 and g.shape == p.shape
+
+
+# ---- compat entry points (the reference extension's names and checks, lncc3d.cu:127-161,253-284,329-344)
+def test_compat_ops_registered_with_reference_names():
+    assert hasattr(torch.ops.fused_lncc, "forward")
+    assert hasattr(torch.ops.fused_lncc, "backward")
+
+
+def test_compat_fakes_fp32_maps_and_pred_dtype_grad():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        p = torch.empty(2, 8, 8, 8, dtype=torch.bfloat16)
+        maps = torch.ops.fused_lncc.forward(p, p, 7, 1e-5)
+        assert len(maps) == 4 and all(m.dtype == torch.float32 and m.shape == p.shape for m in maps)
+        g = torch.ops.fused_lncc.backward(maps[1], maps[2], maps[3], p, p, 7, 1.0)
+        assert g.dtype == torch.bfloat16 and g.shape == p.shape
+
+
+def test_compat_checks_raise_runtime_error():
+    from fused_lncc import compat
+    x = torch.zeros(2, 4, 4, 4)
+    with pytest.raises(RuntimeError, match="contiguous 4D CUDA"):
+        compat.lncc_forward(x, x, 3, 1e-5)
+    with pytest.raises(RuntimeError, match="contiguous 4D fp32 CUDA"):
+        compat.lncc_backward(x, x, x, x, x, 3, 1.0)
+    with pytest.raises(RuntimeError, match="contiguous 4D fp32 CUDA"):
+        compat.box3d_sep_forward(x, 3)
+    with pytest.raises(RuntimeError):
+        compat.lncc_forward(torch.zeros(1, 2, 4, 4, 4), torch.zeros(1, 2, 4, 4, 4), 3, 1e-5)
