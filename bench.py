@@ -424,8 +424,9 @@ def main():
         peak, peak_src = measured_peak_gbs()
         bpv = BYTES_PER_VOXEL[dtype]
         achieved = vox_local * bpv / (result["ms_kernel"] * 1e-3) / 1e9   # GB/s, rank 0's launch
-        # which kernel the library picks for this shape (the band kernel's conditions, include/lncc.h)
-        kname = ("lncc_band_kernel" if (W <= 128 and W % 4 == 0 and H <= 256) else "lncc_sweep_kernel")
+        # which kernel the library picks for this shape (automatic choice, include/lncc.h): the
+        # warp-specialised cluster kernel whenever W % 4 == 0 (torch allocations are aligned)
+        kname = "lncc_ws_kernel" if W % 4 == 0 else "lncc_sweep_kernel"
         traffic = profile_traffic(kname, args.workload) if world == 1 else None
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,

@@ -36,6 +36,7 @@
 
 #include "lncc_band.cuh"
 #include "lncc_compat.cuh"
+#include "lncc_ws.cuh"
 
 namespace lncc {
 
@@ -468,7 +469,7 @@ static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
 // ------------------------------------------------------------------------------------------------
 // band kernel host side
 // ------------------------------------------------------------------------------------------------
-static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band
+static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band, 3 warp-specialised
 
 // Row segments per column in the band kernel's column phases (threads = 128 * segments).
 // LNCC_BAND_SEGMENTS=2|4 overrides the default (a tuning knob; both variants compute the same).
@@ -582,7 +583,7 @@ static BandPlan make_band_plan(int64_t B, int64_t H, int64_t W, int k, int dtype
                                int64_t z_end, const void* p, const void* t, const void* g) {
   BandPlan bp{false, k / 2, 0, 0, 0, nullptr};
   const int choice = g_kernel_choice.load();
-  if (choice == 1) return bp;
+  if (choice == 1 || choice == 3) return bp;
   if (!band_supported(H, W, dtype, p, t, g)) return bp;
   const void* fn = nullptr;
   if (band_kernel_fn(k / 2, dtype, grad, &fn) != cudaSuccess) return bp;
@@ -619,6 +620,156 @@ static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cud
   cfg.stream = st;
   void* args[] = {const_cast<band::BandArgs*>(&ba)};
   return cudaLaunchKernelExC(&cfg, bp.fn, args);
+}
+
+// ------------------------------------------------------------------------------------------------
+// warp-specialised cluster kernel host side (lncc_ws.cuh)
+// ------------------------------------------------------------------------------------------------
+constexpr int kWsMaxCluster = 8;  // portable cluster size; taller planes are cut into row tiles
+
+// W % 4 == 0 and 16-byte (fp32) / 8-byte (bf16) aligned base pointers: the kernel moves 4-column chunks.
+static bool ws_supported(int64_t W, int dtype, const void* p, const void* t, const void* g) {
+  if ((W % 4) != 0) return false;
+  const uintptr_t al = dtype == LNCC_F32 ? 16 : 8;
+  if ((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al))) return false;
+  return true;
+}
+
+template <int R, typename S, bool GRAD>
+static cudaError_t ws_prepare(const void** fn_out) {
+  auto kfn = ws::lncc_ws_kernel<R, S, GRAD>;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, ws::smem_bytes<R>());
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  *fn_out = reinterpret_cast<const void*>(kfn);
+  return cudaSuccess;
+}
+
+template <typename S, bool GRAD>
+static cudaError_t ws_fn_r(int R, const void** fn) {
+  switch (R) {
+    case 1: return ws_prepare<1, S, GRAD>(fn);
+    case 2: return ws_prepare<2, S, GRAD>(fn);
+    case 3: return ws_prepare<3, S, GRAD>(fn);
+    case 4: return ws_prepare<4, S, GRAD>(fn);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static cudaError_t ws_kernel_fn(int R, int dtype, bool grad, const void** fn) {
+  if (dtype == LNCC_F32) return grad ? ws_fn_r<float, true>(R, fn) : ws_fn_r<float, false>(R, fn);
+  return grad ? ws_fn_r<__nv_bfloat16, true>(R, fn) : ws_fn_r<__nv_bfloat16, false>(R, fn);
+}
+
+static int ws_smem_for(int R) {
+  switch (R) {
+    case 1: return ws::smem_bytes<1>();
+    case 2: return ws::smem_bytes<2>();
+    case 3: return ws::smem_bytes<3>();
+    default: return ws::smem_bytes<4>();
+  }
+}
+
+static int ws_max_clusters(const void* fn, int cy, int R) {
+  static std::mutex mu;
+  struct Key { int dev; int cy; const void* fn; int val; };
+  static Key cache[128];
+  static int ncache = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < ncache; ++i)
+    if (cache[i].dev == dev && cache[i].cy == cy && cache[i].fn == fn) return cache[i].val;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(cy);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(unsigned(cy), 1, 1);
+  cfg.blockDim = dim3(ws::NT, 1, 1);
+  cfg.dynamicSmemBytes = size_t(ws_smem_for(R));
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (ncache < 128) cache[ncache++] = {dev, cy, fn, n};
+  return n;
+}
+
+struct WsPlan {
+  bool ok;
+  int R;
+  int cy;
+  int tiles_x, tiles_y;
+  int64_t total;
+  int64_t nclusters;
+  int64_t ipc;
+  const void* fn;
+};
+
+static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bool grad, int64_t z_begin,
+                           int64_t z_end, const void* p, const void* t, const void* g) {
+  WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr};
+  const int choice = g_kernel_choice.load();
+  if (choice == 1 || choice == 2) return wp;
+  if (!ws_supported(W, dtype, p, t, g)) return wp;
+  const void* fn = nullptr;
+  if (ws_kernel_fn(k / 2, dtype, grad, &fn) != cudaSuccess) {
+    cudaGetLastError();
+    return wp;
+  }
+  const int R = k / 2;
+  int cy = int((H + ws::TY - 1) / ws::TY);
+  if (cy > kWsMaxCluster) cy = kWsMaxCluster;
+  const int span_y = ws::TY * cy;
+  const int tx = ws::tile_count(int(W), ws::SPAN, R, 4);
+  const int ty = ws::tile_count(int(H), span_y, R, 1);
+  const int maxc = ws_max_clusters(fn, cy, R);
+  if (maxc < 1) return wp;
+  const int64_t total = B * int64_t(tx) * ty * (z_end - z_begin);
+  const int64_t min_ipc = 32;
+  int64_t nc = (total + min_ipc - 1) / min_ipc;
+  if (nc > maxc) nc = maxc;
+  if (nc < 1) nc = 1;
+  const int64_t ipc = (total + nc - 1) / nc;
+  nc = (total + ipc - 1) / ipc;
+  wp.ok = true;
+  wp.cy = cy;
+  wp.tiles_x = tx;
+  wp.tiles_y = ty;
+  wp.total = total;
+  wp.nclusters = nc;
+  wp.ipc = ipc;
+  wp.fn = fn;
+  return wp;
+}
+
+static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(wp.cy);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(unsigned(wp.cy), unsigned(wp.nclusters), 1);
+  cfg.blockDim = dim3(ws::NT, 1, 1);
+  cfg.dynamicSmemBytes = size_t(ws_smem_for(wp.R));
+  cfg.stream = st;
+  void* args[] = {const_cast<ws::Args*>(&wa)};
+  return cudaLaunchKernelExC(&cfg, wp.fn, args);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -710,6 +861,11 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
   // enough for either kernel (the choice also depends on pointer alignment, known only at launch)
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
   size_t need = size_t(pl.nblocks) * sizeof(double);
+  for (int gflag = 0; gflag < 2; ++gflag) {
+    const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, gflag != 0, z_begin, z_end, nullptr, nullptr, nullptr);
+    if (wp.ok && size_t(wp.cy) * size_t(wp.nclusters) * sizeof(double) > need)
+      need = size_t(wp.cy) * size_t(wp.nclusters) * sizeof(double);
+  }
   const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, true, z_begin, z_end, nullptr, nullptr, nullptr);
   if (bp.ok) {
     const size_t nb = size_t(bp.cy) * size_t(bp.nclusters) * sizeof(double);
@@ -737,8 +893,10 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     return LNCC_ERR_BAD_ARG;
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
   if (pl.nblocks > INT32_MAX) return LNCC_ERR_TOO_LARGE;
-  const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
-  const int64_t nparts = bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
+  const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
+  BandPlan bp{false, kernel_size / 2, 0, 0, 0, nullptr};
+  if (!wp.ok) bp = make_band_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
+  const int64_t nparts = wp.ok ? int64_t(wp.cy) * wp.nclusters : bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
   const size_t need = size_t(nparts) * sizeof(double);
   if (!workspace || workspace_bytes < need || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
   if (loss_out && !(loss_count > 0.0)) return LNCC_ERR_BAD_ARG;
@@ -770,7 +928,28 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
 
   cudaError_t e;
   const bool g = grad != nullptr;
-  if (bp.ok) {
+  if (wp.ok) {
+    ws::Args wa;
+    wa.p = pred;
+    wa.t = target;
+    wa.g = grad;
+    wa.partials = a.partials;
+    wa.gscale_dev = grad_scale_dev;
+    wa.gscale = grad_scale;
+    wa.n = a.n;
+    wa.dr = smooth_dr;
+    wa.D = int(D);
+    wa.H = int(H);
+    wa.W = int(W);
+    wa.z_begin = int(z_begin);
+    wa.z_end = int(z_end);
+    wa.tiles_x = wp.tiles_x;
+    wa.tiles_y = wp.tiles_y;
+    wa.span_y = ws::TY * wp.cy;
+    wa.total_items = wp.total;
+    wa.items_per_cluster = wp.ipc;
+    e = launch_ws(wp, wa, stream);
+  } else if (bp.ok) {
     band::BandArgs ba;
     ba.p = pred;
     ba.t = target;
@@ -820,7 +999,7 @@ int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype, 
 }
 
 int lncc_select_kernel(int which) {
-  if (which < 0 || which > 2) return LNCC_ERR_BAD_ARG;
+  if (which < 0 || which > 3) return LNCC_ERR_BAD_ARG;
   g_kernel_choice.store(which);
   return LNCC_OK;
 }

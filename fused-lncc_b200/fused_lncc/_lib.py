@@ -100,9 +100,11 @@ def check(status, what):
         raise RuntimeError(f"{what}: {strerror(status)} (status {status})")
 
 
-KERNEL_AUTO, KERNEL_SWEEP, KERNEL_BAND = 0, 1, 2
+KERNEL_AUTO, KERNEL_SWEEP, KERNEL_BAND, KERNEL_WS = 0, 1, 2, 3
 
 
 def select_kernel(which):
-    """Process-wide kernel choice (0 auto, 1 general sweep kernel, 2 band kernel where supported)."""
+    """Process-wide kernel choice: 0 auto (warp-specialised cluster kernel where it applies, else the
+    band kernel, else the general sweep kernel), 1 general sweep kernel, 2 band kernel where supported,
+    3 warp-specialised cluster kernel where supported."""
     check(load().lncc_select_kernel(int(which)), "lncc_select_kernel")

@@ -148,9 +148,11 @@ int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_
 
 /*
  * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:
- * the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the pointers are 16-byte
- * aligned, else the general sweep kernel), 1 = always the general sweep kernel, 2 = band kernel
- * where supported (as 0). No counterpart in the reference, which has a single kernel per step.
+ * the warp-specialised cluster kernel when W % 4 == 0 and the pointers are 16-byte (fp32) / 8-byte
+ * (bf16) aligned, else the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the
+ * pointers are 16-byte aligned, else the general sweep kernel), 1 = always the general sweep
+ * kernel, 2 = band kernel where supported, 3 = warp-specialised kernel where supported. No
+ * counterpart in the reference, which has a single kernel per step.
  */
 int lncc_select_kernel(int which);
 

@@ -274,11 +274,11 @@ def test_plane_range_matches_whole_volume():
     assert abs(parts - s_full.item()) < 1e-6 * max(1.0, abs(s_full.item()))
 
 
-# ---- both kernels: the cluster band kernel (default where it applies) and the general sweep ---------
-@pytest.fixture(params=["sweep", "band"])
+# ---- every kernel: the warp-specialised cluster kernel (default), the band kernel, the general sweep --
+@pytest.fixture(params=["sweep", "band", "ws"])
 def kernel(request):
     from fused_lncc import _lib
-    _lib.select_kernel(_lib.KERNEL_SWEEP if request.param == "sweep" else _lib.KERNEL_AUTO)
+    _lib.select_kernel({"sweep": _lib.KERNEL_SWEEP, "band": _lib.KERNEL_BAND, "ws": _lib.KERNEL_WS}[request.param])
     yield request.param
     _lib.select_kernel(_lib.KERNEL_AUTO)
 
@@ -297,16 +297,59 @@ def test_band_equals_sweep_blurred(k):
     from fused_lncc import _lib, synth
     pred, target = synth.blurred_pair((2, 2, 48, 64, 128), device="cuda")
     outs = []
-    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_AUTO):
+    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_BAND, _lib.KERNEL_WS):
         _lib.select_kernel(which)
         try:
             outs.append(fused(pred, target, k))
         finally:
             _lib.select_kernel(_lib.KERNEL_AUTO)
-    (l1, g1), (l2, g2) = outs
-    assert abs(l1 - l2) < 1e-6
+    (l1, g1) = outs[0]
+    for l2, g2 in outs[1:]:
+        assert abs(l1 - l2) < 1e-6
+        cos, rel = cos_rel(g2, g1)
+        assert cos > 0.999999 and rel < 1e-4, (cos, rel)
+
+
+# tiled planes (W > 128 or H > 128: overlapping spans) and odd sizes through the warp-specialised kernel
+@pytest.mark.parametrize("shape,k", [((1, 1, 20, 40, 224), 9), ((1, 1, 24, 200, 200), 7), ((1, 1, 33, 130, 16), 5),
+                                     ((1, 1, 6, 256, 16), 3), ((1, 1, 3, 2, 4), 7), ((2, 1, 17, 260, 12), 3)])
+def test_ws_tiled_matches_sweep(shape, k):
+    from fused_lncc import _lib
+    g = torch.Generator().manual_seed(sum(shape) * 7 + k)
+    p = torch.randn(*shape, generator=g).cuda()
+    t = torch.randn(*shape, generator=g).cuda()
+    outs = []
+    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_WS):
+        _lib.select_kernel(which)
+        try:
+            s = torch.zeros((), dtype=torch.float64, device="cuda")
+            _, gr = lncc_fused(p, t, k, grad_scale=1.0, cc_sum_out=s)
+            torch.cuda.synchronize()
+            outs.append((s.item(), gr.float()))
+        finally:
+            _lib.select_kernel(_lib.KERNEL_AUTO)
+    (s1, g1), (s2, g2) = outs
+    assert abs(s1 - s2) < 1e-6 * max(1.0, abs(s1)) + 1e-9 * p.numel(), (s1, s2)
     cos, rel = cos_rel(g2, g1)
-    assert cos > 0.999999 and rel < 1e-4, (cos, rel)
+    assert cos > 0.999999 and rel < 1e-5, (cos, rel)
+
+
+def test_ws_repeat_bitwise():
+    """Many launches of the mbarrier-paced kernel give bitwise identical loss and gradient."""
+    from fused_lncc import _lib, synth
+    pred, target = synth.blurred_pair((2, 2, 48, 128, 128), device="cuda")
+    _lib.select_kernel(_lib.KERNEL_WS)
+    try:
+        s0 = torch.zeros((), dtype=torch.float64, device="cuda")
+        _, g0 = lncc_fused(pred, target, 7, cc_sum_out=s0)
+        s = torch.zeros_like(s0)
+        g = torch.empty_like(g0)
+        for _ in range(50):
+            lncc_fused(pred, target, 7, cc_sum_out=s, out=g)
+        torch.cuda.synchronize()
+        assert s.item() == s0.item() and torch.equal(g, g0)
+    finally:
+        _lib.select_kernel(_lib.KERNEL_AUTO)
 
 
 def test_band_bf16_and_loss_only():
