@@ -11,9 +11,9 @@
 //                    tensor memory (TMEM), updated with the raw plane entering and the one leaving the
 //                    window (both loaded one step ahead), boxes them along W with warp shuffles and
 //                    stores them (DW) for the step's stat plane. The CTA's first and last 2r rows are
-//                    then sent to the neighbouring CTAs' halo rows by one bulk copy each (TMA engine,
-//                    completion counted in bytes on the receiver's barrier), so no CTA recomputes
-//                    another CTA's rows and no thread waits for the transfer.
+//                    then sent to the neighbouring CTAs' halo rows by bulk copies (TMA engine, one per
+//                    warp and neighbour, completion counted in bytes on the receiver's barrier), so no
+//                    CTA recomputes another CTA's rows.
 //   BC  (warps 4-11) two threads per column, each for half of the CTA's rows: H box of DW over
 //                    8 + 4r rows -> the five window sums -> cc (loss partial) and the three adjoint
 //                    fields on 8 + 2r rows -> H box of the adjoints -> AH for its 8 rows.
@@ -281,21 +281,6 @@ __device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
   return r;
 }
 
-// Named barrier 1 over the A group's 128 threads with an OR reduction of `pred`: every A thread gets
-// the same answer, so the group can leave its loop together.
-__device__ __forceinline__ bool bar_red_or_a(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred P, Q;\n\t"
-      "setp.ne.u32 P, %1, 0;\n\t"
-      "bar.red.or.pred Q, 1, 128, P;\n\t"
-      "selp.u32 %0, 1, 0, Q;\n\t}"
-      : "=r"(r)
-      : "r"(pred ? 1u : 0u)
-      : "memory");
-  return r != 0;
-}
-
 // Empty asm naming a float4 as read-write: arithmetic on it cannot be scheduled before this point, so
 // loads issued early (prefetch) are not waited for earlier than intended.
 __device__ __forceinline__ void reg_fence(float4& v) {
@@ -427,8 +412,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
 
   const float nf = a.n, nh = 0.5f * a.n, ndr = a.n * a.dr;
   double acc = 0.0;  // BC: loss partial
-  // After a timed-out wait (a protocol error) every role leaves its loops without arriving on any
-  // barrier again: the A group decides together (bar_red_or_a), the other warps each warp-uniformly.
+  // After a timed-out wait (a protocol error) every warp leaves its loops (warp-uniformly) without
+  // arriving on any barrier or sending any copy again.
   bool a_aborted = false;
 
   // Segment walk shared by every role: the same (volume, tile, plane range) sequence and the same
@@ -552,6 +537,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         Raw r;
         load_raw(more && zi < D, zi, more && zo >= 0, zo, r);
         mbar_wait(bar(BAR_DW_EMPTY, i), ((s >> 1) & 1u) ^ 1u, abort_flag);
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+          a_aborted = true;
+          break;
+        }
         if (cvalid) {
           // W box of each field -> the CTA's own DW rows
           tm_wait_st();
@@ -563,31 +552,33 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
             wbox16<R>(v, q, [&](int j, float4 w4) { sts4(own + uint32_t(f * SPAN * 4) + choff[j], w4); });
           }
         }
-        // make the rows visible to the bulk-copy (async) proxy; the barrier also tells every A thread
-        // whether any wait of the CTA timed out, so the A warps leave together
+        // make this warp's rows visible to the bulk-copy (async) proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (bar_red_or_a(*abort_flag != 0)) {
-          a_aborted = true;
-          break;
-        }
         __syncwarp();
         if (lane == 0) {
           // warp 0 also announces the halo bytes the neighbours send into this CTA for this step
           if (warp == 0) mbar_arrive_expect_tx(bar(BAR_DW_FULL, i), rx_bytes);
           else mbar_arrive_cta(bar(BAR_DW_FULL, i));
-        }
-        // Halo rows to the neighbours, all five fields in one copy each: my first 2R rows become the
-        // CTA above's rows [TY + 2R, TY + 4R), my last 2R rows the CTA below's rows [0, 2R). Sent on
-        // every step, also for planes outside the volume (whose rows nobody reads): a neighbour's
-        // column groups can then never run two steps ahead of this CTA, because their step-s+2 input
-        // includes this copy, which is issued only after this CTA's step-s buffer was released.
-        if (tid == 0) {
-          if (has_up)
-            bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][TY + 2 * R][0][0]), uint32_t(rank - 1)),
-                              smem_addr(&sm.dw[i][2 * R][0][0]), kHaloBytes, mapa_rank(bar(BAR_DW_FULL, i), uint32_t(rank - 1)));
-          if (has_dn)
-            bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][0][0][0]), uint32_t(rank + 1)),
-                              smem_addr(&sm.dw[i][TY][0][0]), kHaloBytes, mapa_rank(bar(BAR_DW_FULL, i), uint32_t(rank + 1)));
+          // Halo rows to the neighbours, each warp its own rows (all five fields of a row are
+          // contiguous): the CTA's first 2R rows become the CTA above's rows [TY + 2R, TY + 4R), its
+          // last 2R rows the CTA below's rows [0, 2R). Sent on every step, also for planes outside the
+          // volume (whose rows nobody reads): a neighbour's column groups can then never run two steps
+          // ahead of this CTA, because their step-s+2 input includes these copies, which are issued
+          // only after this CTA's step-s buffer was released.
+          const int r0 = 4 * warp, r1 = 4 * warp + 4;  // this warp's rows
+          constexpr uint32_t kRowBytes = 5 * SPAN * 4;
+          if (has_up && r0 < 2 * R) {
+            const int e1 = r1 < 2 * R ? r1 : 2 * R;
+            bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][TY + 2 * R + r0][0][0]), uint32_t(rank - 1)),
+                              smem_addr(&sm.dw[i][2 * R + r0][0][0]), uint32_t(e1 - r0) * kRowBytes,
+                              mapa_rank(bar(BAR_DW_FULL, i), uint32_t(rank - 1)));
+          }
+          if (has_dn && r1 > TY - 2 * R) {
+            const int b0 = r0 > TY - 2 * R ? r0 : TY - 2 * R;
+            bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][b0 - (TY - 2 * R)][0][0]), uint32_t(rank + 1)),
+                              smem_addr(&sm.dw[i][2 * R + b0][0][0]), uint32_t(r1 - b0) * kRowBytes,
+                              mapa_rank(bar(BAR_DW_FULL, i), uint32_t(rank + 1)));
+          }
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -794,10 +785,14 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
             }
             if (cvalid) {
               box_ah(i, f, [&](int j, float4 w4) {
-                sum[4 * j] += w4.x - old[4 * j];
-                sum[4 * j + 1] += w4.y - old[4 * j + 1];
-                sum[4 * j + 2] += w4.z - old[4 * j + 2];
-                sum[4 * j + 3] += w4.w - old[4 * j + 3];
+                const float2 lo = add2(make_float2(sum[4 * j], sum[4 * j + 1]),
+                                       sub2(make_float2(w4.x, w4.y), make_float2(old[4 * j], old[4 * j + 1])));
+                const float2 hi = add2(make_float2(sum[4 * j + 2], sum[4 * j + 3]),
+                                       sub2(make_float2(w4.z, w4.w), make_float2(old[4 * j + 2], old[4 * j + 3])));
+                sum[4 * j] = lo.x;
+                sum[4 * j + 1] = lo.y;
+                sum[4 * j + 2] = hi.x;
+                sum[4 * j + 3] = hi.y;
                 tm_st4(ring + uint32_t(4 * j), w4);
               });
             } else {

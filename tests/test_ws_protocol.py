@@ -1,7 +1,8 @@
 """CPU model of the warp-specialised kernel's mbarrier protocol (fused-lncc_b200/csrc/lncc_ws.cuh).
 
 One cluster of CTAs; per CTA 4 A warps, 8 BC warps and 4 D warps walk the same step sequence with random
-work times, and the halo bulk copies land after random delays. Barriers are modelled like mbarriers
+work times, and the halo bulk copies (one per A warp: warps 0-1 to the CTA above, 2-3 below) land after
+random delays. Barriers are modelled like mbarriers
 (arrival count, pending count, transaction bytes, phase). Every arrival and every completed copy is
 tagged with the phase it is meant for; a tag different from the barrier's current phase is a protocol
 violation (the hardware would count it silently in the wrong phase), and actors left waiting at the end
@@ -85,10 +86,10 @@ def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
             send = always_send or valid
             ntx = HALO * ((j > 0) + (j < ncta - 1))
             arrive((j, "full", i), u, tx=(ntx if (w == 0 and send) else 0))
-            if w == 0 and send:
-                for nb in (j - 1, j + 1):
-                    if 0 <= nb < ncta:
-                        at(t[0] + rnd.expovariate(0.5), lambda nb=nb, i=i, u=u: complete_tx((nb, "full", i), u, HALO))
+            # each warp sends its own halo rows: warps 0, 1 to the CTA above, warps 2, 3 below
+            nb = j - 1 if w < 2 else j + 1
+            if send and 0 <= nb < ncta:
+                at(t[0] + rnd.expovariate(0.5), lambda nb=nb, i=i, u=u: complete_tx((nb, "full", i), u, HALO // 2))
 
     def BC(j, w):
         for s in range(nsteps):
