@@ -627,17 +627,22 @@ static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cud
 // ------------------------------------------------------------------------------------------------
 constexpr int kWsMaxCluster = 8;  // portable cluster size; taller planes are cut into row tiles
 
-// W % 4 == 0 and 16-byte (fp32) / 8-byte (bf16) aligned base pointers: the kernel moves 4-column chunks.
-static bool ws_supported(int64_t W, int dtype, const void* p, const void* t, const void* g) {
-  if ((W % 4) != 0) return false;
-  const uintptr_t al = dtype == LNCC_F32 ? 16 : 8;
-  if ((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al))) return false;
-  return true;
+// Global-memory chunk width of the kernel for this call: 8 columns (256-bit fp32 / 128-bit bf16
+// accesses) when W % 8 == 0 and the base pointers are aligned to a chunk, else 4 columns when
+// W % 4 == 0 and aligned to that; 0 = the kernel does not apply.
+static int ws_chunk(int64_t W, int dtype, const void* p, const void* t, const void* g) {
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  auto aligned = [&](uintptr_t al) {
+    return !((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al)));
+  };
+  if (W % 8 == 0 && aligned(8 * esz)) return 8;
+  if (W % 4 == 0 && aligned(4 * esz)) return 4;
+  return 0;
 }
 
-template <int R, typename S, bool GRAD>
+template <int R, typename S, bool GRAD, int CW>
 static cudaError_t ws_prepare(const void** fn_out) {
-  auto kfn = ws::lncc_ws_kernel<R, S, GRAD>;
+  auto kfn = ws::lncc_ws_kernel<R, S, GRAD, CW>;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -652,20 +657,25 @@ static cudaError_t ws_prepare(const void** fn_out) {
   return cudaSuccess;
 }
 
-template <typename S, bool GRAD>
+template <typename S, bool GRAD, int CW>
 static cudaError_t ws_fn_r(int R, const void** fn) {
   switch (R) {
-    case 1: return ws_prepare<1, S, GRAD>(fn);
-    case 2: return ws_prepare<2, S, GRAD>(fn);
-    case 3: return ws_prepare<3, S, GRAD>(fn);
-    case 4: return ws_prepare<4, S, GRAD>(fn);
+    case 1: return ws_prepare<1, S, GRAD, CW>(fn);
+    case 2: return ws_prepare<2, S, GRAD, CW>(fn);
+    case 3: return ws_prepare<3, S, GRAD, CW>(fn);
+    case 4: return ws_prepare<4, S, GRAD, CW>(fn);
     default: return cudaErrorInvalidValue;
   }
 }
 
-static cudaError_t ws_kernel_fn(int R, int dtype, bool grad, const void** fn) {
-  if (dtype == LNCC_F32) return grad ? ws_fn_r<float, true>(R, fn) : ws_fn_r<float, false>(R, fn);
-  return grad ? ws_fn_r<__nv_bfloat16, true>(R, fn) : ws_fn_r<__nv_bfloat16, false>(R, fn);
+template <typename S, bool GRAD>
+static cudaError_t ws_fn_cw(int R, int cw, const void** fn) {
+  return cw == 8 ? ws_fn_r<S, GRAD, 8>(R, fn) : ws_fn_r<S, GRAD, 4>(R, fn);
+}
+
+static cudaError_t ws_kernel_fn(int R, int dtype, bool grad, int cw, const void** fn) {
+  if (dtype == LNCC_F32) return grad ? ws_fn_cw<float, true>(R, cw, fn) : ws_fn_cw<float, false>(R, cw, fn);
+  return grad ? ws_fn_cw<__nv_bfloat16, true>(R, cw, fn) : ws_fn_cw<__nv_bfloat16, false>(R, cw, fn);
 }
 
 static int ws_smem_for(int R) {
@@ -723,9 +733,12 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr};
   const int choice = g_kernel_choice.load();
   if (choice == 1 || choice == 2) return wp;
-  if (!ws_supported(W, dtype, p, t, g)) return wp;
+  // pointers unknown (workspace query): plan as for aligned tensors
+  const int cw = (p == nullptr && t == nullptr) ? ((W % 8 == 0) ? 8 : (W % 4 == 0) ? 4 : 0)
+                                                 : ws_chunk(W, dtype, p, t, g);
+  if (cw == 0) return wp;
   const void* fn = nullptr;
-  if (ws_kernel_fn(k / 2, dtype, grad, &fn) != cudaSuccess) {
+  if (ws_kernel_fn(k / 2, dtype, grad, cw, &fn) != cudaSuccess) {
     cudaGetLastError();
     return wp;
   }
@@ -733,7 +746,7 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   int cy = int((H + ws::TY - 1) / ws::TY);
   if (cy > kWsMaxCluster) cy = kWsMaxCluster;
   const int span_y = ws::TY * cy;
-  const int tx = ws::tile_count(int(W), ws::SPAN, R, 4);
+  const int tx = ws::tile_count(int(W), ws::SPAN, R, cw);
   const int ty = ws::tile_count(int(H), span_y, R, 1);
   const int maxc = ws_max_clusters(fn, cy, R);
   if (maxc < 1) return wp;

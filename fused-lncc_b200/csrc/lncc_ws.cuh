@@ -135,6 +135,59 @@ struct IO<__nv_bfloat16> {
   }
 };
 
+// Chunk of CW = 4 or 8 consecutive elements <-> CW/4 float4. CW = 8 uses one 256-bit access for fp32
+// (ld/st .v8.f32, 32-byte aligned) and one 128-bit access for bf16: with 16 columns per lane, a lane's
+// two 8-column chunks fill whole 32-byte sectors, where 4-column chunks fill only half of each.
+template <typename S, int CW>
+struct Chunk;
+template <>
+struct Chunk<float, 4> {
+  static __device__ __forceinline__ void ld(const float* p, float4* o) { o[0] = IO<float>::ld(p); }
+  static __device__ __forceinline__ void st(float* p, const float4* v) { IO<float>::st(p, v[0]); }
+};
+template <>
+struct Chunk<__nv_bfloat16, 4> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float4* o) { o[0] = IO<__nv_bfloat16>::ld(p); }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float4* v) { IO<__nv_bfloat16>::st(p, v[0]); }
+};
+template <>
+struct Chunk<float, 8> {
+  static __device__ __forceinline__ void ld(const float* p, float4* o) {
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(o[0].x), "=f"(o[0].y), "=f"(o[0].z), "=f"(o[0].w), "=f"(o[1].x), "=f"(o[1].y), "=f"(o[1].z),
+                   "=f"(o[1].w)
+                 : "l"(p));
+  }
+  static __device__ __forceinline__ void st(float* p, const float4* v) {
+    asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v[0].x), "f"(v[0].y), "f"(v[0].z),
+                 "f"(v[0].w), "f"(v[1].x), "f"(v[1].y), "f"(v[1].z), "f"(v[1].w)
+                 : "memory");
+  }
+};
+template <>
+struct Chunk<__nv_bfloat16, 8> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float4* o) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * h]));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * h + 1]));
+      o[h] = make_float4(a.x, a.y, b.x, b.y);
+    }
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float4* v) {
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(v[h].x, v[h].y), b = __floats2bfloat162_rn(v[h].z, v[h].w);
+      w[2 * h] = *reinterpret_cast<uint32_t*>(&a);
+      w[2 * h + 1] = *reinterpret_cast<uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
 // ---- packed f32x2 arithmetic (sm_100) ------------------------------------------------------------------
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
@@ -362,8 +415,9 @@ struct Seg {
   int xb, ox0, ox1;  // span column origin, output columns
 };
 
-template <int R, typename S, bool GRAD>
+template <int R, typename S, bool GRAD, int CW>
 __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
+  constexpr int NCH = VW / CW;  // global-memory chunks per lane
   constexpr int K = Geo<R>::K, ER = Geo<R>::ER;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   using SM = Smem<R>;
@@ -433,7 +487,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       const int tx = int(item % a.tiles_x);
       const int ty = int((item / a.tiles_x) % a.tiles_y);
       sg.b = item / (int64_t(a.tiles_x) * a.tiles_y);
-      tile_geom(tx, W, SPAN, R, 4, sg.xb, sg.ox0, sg.ox1);
+      tile_geom(tx, W, SPAN, R, CW, sg.xb, sg.ox0, sg.ox1);
       tile_geom(ty, H, a.span_y, R, 1, sg.yb, sg.oy0, sg.oy1);
     }
     const int nsteps = sg.ze - sg.zs + 2 * R;
@@ -446,10 +500,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       const int yl = warp * 4 + (lane >> 3), q = lane & 7;
       const int Y = sg.yb + rank * TY + yl;
       const int X0 = sg.xb + VW * q;
-      uint32_t cm = 0;  // valid 4-column chunks (W % 4 == 0 and X0 % 4 == 0: all or nothing)
+      uint32_t cm = 0;  // valid CW-column chunks (W % CW == 0 and X0 % CW == 0: all or nothing)
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (Y >= 0 && Y < H && X0 + 4 * j >= 0 && X0 + 4 * j < W) cm |= 1u << j;
+      for (int j = 0; j < NCH; ++j)
+        if (Y >= 0 && Y < H && X0 + CW * j >= 0 && X0 + CW * j < W) cm |= 1u << j;
       const int64_t roff = (cm ? int64_t(Y) * W + X0 : 0);
       const uint32_t tmA = sm.tmem_base + (uint32_t(32 * (warp & 3)) << 16) + Geo<R>::TM_A;
       uint32_t choff[4];  // byte offsets of this lane's four 4-column chunks in a swizzled row
@@ -461,13 +515,24 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         float4 pi[4], ti[4], po[4], to[4];
       };
       auto load_raw = [&](bool in_ok, int zi, bool out_ok, int zo, Raw& r) {
+        constexpr int Q = CW / 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < NCH; ++j) {
           const bool cj = (cm >> j) & 1u;
-          r.pi[j] = (in_ok && cj) ? IO<S>::ld(P + zi * HW + roff + 4 * j) : z4;
-          r.ti[j] = (in_ok && cj) ? IO<S>::ld(T + zi * HW + roff + 4 * j) : z4;
-          r.po[j] = (out_ok && cj) ? IO<S>::ld(P + zo * HW + roff + 4 * j) : z4;
-          r.to[j] = (out_ok && cj) ? IO<S>::ld(T + zo * HW + roff + 4 * j) : z4;
+          if (in_ok && cj) {
+            Chunk<S, CW>::ld(P + zi * HW + roff + CW * j, &r.pi[Q * j]);
+            Chunk<S, CW>::ld(T + zi * HW + roff + CW * j, &r.ti[Q * j]);
+          } else {
+#pragma unroll
+            for (int h = 0; h < Q; ++h) r.pi[Q * j + h] = r.ti[Q * j + h] = z4;
+          }
+          if (out_ok && cj) {
+            Chunk<S, CW>::ld(P + zo * HW + roff + CW * j, &r.po[Q * j]);
+            Chunk<S, CW>::ld(T + zo * HW + roff + CW * j, &r.to[Q * j]);
+          } else {
+#pragma unroll
+            for (int h = 0; h < Q; ++h) r.po[Q * j + h] = r.to[Q * j + h] = z4;
+          }
         }
       };
       // D update of the five running sums (TMEM, 16 columns per field) with a Raw pair of planes.
@@ -709,11 +774,11 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       const int yl = (warp - 12) * 4 + (lane >> 3), q = lane & 7;
       const int Y = sg.yb + rank * TY + yl;
       const int X0 = sg.xb + VW * q;
-      uint32_t om = 0;  // output chunks
+      uint32_t om = 0;  // output CW-column chunks
       if (Y >= sg.oy0 && Y < sg.oy1) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (X0 + 4 * j >= sg.ox0 && X0 + 4 * j < sg.ox1) om |= 1u << j;
+        for (int j = 0; j < NCH; ++j)
+          if (X0 + CW * j >= sg.ox0 && X0 + CW * j < sg.ox1) om |= 1u << j;
       }
       const int64_t roff = om ? int64_t(Y) * W + X0 : 0;
       S* __restrict__ G = reinterpret_cast<S*>(a.g) + sg.b * int64_t(Dout) * HW;
@@ -761,10 +826,15 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           const int i = int(s & 1u);
           float4 pv[4], tv[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const bool v = out_ok && ((om >> j) & 1u);
-            pv[j] = v ? IO<S>::ld(P + o * HW + roff + 4 * j) : z4;
-            tv[j] = v ? IO<S>::ld(T + o * HW + roff + 4 * j) : z4;
+          for (int j = 0; j < NCH; ++j) {
+            constexpr int Q = CW / 4;
+            if (out_ok && ((om >> j) & 1u)) {
+              Chunk<S, CW>::ld(P + o * HW + roff + CW * j, &pv[Q * j]);
+              Chunk<S, CW>::ld(T + o * HW + roff + CW * j, &tv[Q * j]);
+            } else {
+#pragma unroll
+              for (int h = 0; h < Q; ++h) pv[Q * j + h] = tv[Q * j + h] = z4;
+            }
           }
           tm_wait_st();
           mbar_wait(bar(BAR_AH_FULL, i), (s >> 1) & 1u, abort_flag);
@@ -812,9 +882,18 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
             tm_ld16(tsum + 32u, sc);
             if (out_ok) {
               S* gp = G + int64_t(o - a.z_begin) * HW + roff;
+              constexpr int Q = CW / 4;
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                if ((om >> j) & 1u) IO<S>::st(gp + 4 * j, grad4(pv[j], tv[j], sa + 4 * j, sb + 4 * j, sc + 4 * j));
+              for (int j = 0; j < NCH; ++j) {
+                if (!((om >> j) & 1u)) continue;
+                float4 g4[Q];
+#pragma unroll
+                for (int h = 0; h < Q; ++h) {
+                  const int c4 = Q * j + h;
+                  g4[h] = grad4(pv[c4], tv[c4], sa + 4 * c4, sb + 4 * c4, sc + 4 * c4);
+                }
+                Chunk<S, CW>::st(gp + CW * j, g4);
+              }
             }
           }
           slot = (slot + 1 == K) ? 0 : slot + 1;
@@ -863,11 +942,18 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           if (out_ok) {
             S* gp = G + int64_t(o - a.z_begin) * HW + roff;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < NCH; ++j) {
               if (!((om >> j) & 1u)) continue;
-              const float4 p4 = IO<S>::ld(P + o * HW + roff + 4 * j);
-              const float4 t4 = IO<S>::ld(T + o * HW + roff + 4 * j);
-              IO<S>::st(gp + 4 * j, grad4(p4, t4, sum[0] + 4 * j, sum[1] + 4 * j, sum[2] + 4 * j));
+              constexpr int Q = CW / 4;
+              float4 p4[Q], t4[Q], g4[Q];
+              Chunk<S, CW>::ld(P + o * HW + roff + CW * j, p4);
+              Chunk<S, CW>::ld(T + o * HW + roff + CW * j, t4);
+#pragma unroll
+              for (int h = 0; h < Q; ++h) {
+                const int c4 = Q * j + h;
+                g4[h] = grad4(p4[h], t4[h], sum[0] + 4 * c4, sum[1] + 4 * c4, sum[2] + 4 * c4);
+              }
+              Chunk<S, CW>::st(gp + CW * j, g4);
             }
           }
           slot = (slot + 1 == K) ? 0 : slot + 1;

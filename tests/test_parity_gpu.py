@@ -311,8 +311,10 @@ def test_band_equals_sweep_blurred(k):
 
 
 # tiled planes (W > 128 or H > 128: overlapping spans) and odd sizes through the warp-specialised kernel
+# (W % 8 == 0 takes 8-column global accesses, W % 8 == 4 the 4-column ones)
 @pytest.mark.parametrize("shape,k", [((1, 1, 20, 40, 224), 9), ((1, 1, 24, 200, 200), 7), ((1, 1, 33, 130, 16), 5),
-                                     ((1, 1, 6, 256, 16), 3), ((1, 1, 3, 2, 4), 7), ((2, 1, 17, 260, 12), 3)])
+                                     ((1, 1, 6, 256, 16), 3), ((1, 1, 3, 2, 4), 7), ((2, 1, 17, 260, 12), 3),
+                                     ((1, 2, 24, 40, 132), 7), ((1, 1, 30, 48, 252), 9)])
 def test_ws_tiled_matches_sweep(shape, k):
     from fused_lncc import _lib
     g = torch.Generator().manual_seed(sum(shape) * 7 + k)
