@@ -230,11 +230,13 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t
       "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
       : "memory");
 }
+// Acquire at CTA scope, as for any transaction barrier: the barrier is in this CTA's shared memory, and
+// the bytes the neighbours' bulk copies write here are visible once their complete_tx has been counted.
 __device__ __forceinline__ bool mbar_test(uint32_t a, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred P;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, P;\n\t}"
       : "=r"(ok)
       : "r"(a), "r"(parity)
@@ -294,6 +296,21 @@ __device__ __forceinline__ void tm_st16(uint32_t ta, const float (&v)[16]) {
       : "memory");
 }
 __device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 16-column load without the wait; the registers are valid only after tm_wait_ld16 names them.
+__device__ __forceinline__ void tm_ld16_issue(uint32_t ta, uint32_t (&u)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+        "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15])
+      : "r"(ta));
+}
+// Waits for every outstanding TMEM load of the thread; naming the registers keeps their uses after it.
+__device__ __forceinline__ void tm_wait_ld16(uint32_t (&u)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(u[0]), "+r"(u[1]), "+r"(u[2]), "+r"(u[3]), "+r"(u[4]), "+r"(u[5]), "+r"(u[6]),
+                 "+r"(u[7]), "+r"(u[8]), "+r"(u[9]), "+r"(u[10]), "+r"(u[11]), "+r"(u[12]), "+r"(u[13]),
+                 "+r"(u[14]), "+r"(u[15]));
+}
 // 8-column load without the wait; the registers are valid only after tm_wait_ld8 names them.
 __device__ __forceinline__ void tm_ld8_issue(uint32_t ta, uint32_t (&u)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -610,11 +627,18 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           // W box of each field -> the CTA's own DW rows
           tm_wait_st();
           const uint32_t own = smem_addr(&sm.dw[i][2 * R + yl][0][0]);
+          // the next field's TMEM load is in flight while this field is boxed
+          uint32_t ub[2][16];
+          tm_ld16_issue(tmA, ub[0]);
+          tm_wait_ld16(ub[0]);
 #pragma unroll
           for (int f = 0; f < 5; ++f) {
+            if (f + 1 < 5) tm_ld16_issue(tmA + uint32_t(16 * (f + 1)), ub[(f + 1) & 1]);
             float v[16];
-            tm_ld16(tmA + uint32_t(16 * f), v);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) v[m] = __uint_as_float(ub[f & 1][m]);
             wbox16<R>(v, q, [&](int j, float4 w4) { sts4(own + uint32_t(f * SPAN * 4) + choff[j], w4); });
+            if (f + 1 < 5) tm_wait_ld16(ub[(f + 1) & 1]);
           }
         }
         // make this warp's rows visible to the bulk-copy (async) proxy
