@@ -311,20 +311,6 @@ __device__ __forceinline__ void tm_wait_ld16(uint32_t (&u)[16]) {
                  "+r"(u[7]), "+r"(u[8]), "+r"(u[9]), "+r"(u[10]), "+r"(u[11]), "+r"(u[12]), "+r"(u[13]),
                  "+r"(u[14]), "+r"(u[15]));
 }
-// 8-column load without the wait; the registers are valid only after tm_wait_ld8 names them.
-__device__ __forceinline__ void tm_ld8_issue(uint32_t ta, uint32_t (&u)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7])
-               : "r"(ta)
-               : "memory");
-}
-// Waits for every outstanding TMEM load of the thread; naming the registers keeps their uses after it.
-__device__ __forceinline__ void tm_wait_ld8(uint32_t (&u)[8]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(u[0]), "+r"(u[1]), "+r"(u[2]), "+r"(u[3]), "+r"(u[4]), "+r"(u[5]), "+r"(u[6]), "+r"(u[7])
-               :
-               : "memory");
-}
 __device__ __forceinline__ void tm_st8(uint32_t ta, const uint32_t (&u)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta), "r"(u[0]),
                "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
@@ -338,11 +324,6 @@ __device__ __forceinline__ void tm_st4(uint32_t ta, float4 v) {
 
 __device__ __forceinline__ void sts4(uint32_t addr, float4 v) {
   asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-// Store to the shared memory of another CTA of the cluster (address from mapa).
-__device__ __forceinline__ void sts4_cluster(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
 __device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
