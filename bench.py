@@ -3,9 +3,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
-Prints ONE JSON line on rank 0. A step is one forward + backward of the loss through the public API
-over this rank's share of the workload's volumes (N*C volumes split across ranks, weak in the
-sense of fixed total work per N; "scaling" is reported accordingly). Timing: W untimed warm-up steps,
+Prints ONE JSON line on rank 0. A step is one forward + backward of the loss through the public API.
+Volume workloads scale weakly: every rank owns a full batch of the workload's N*C volumes (its own
+seed), the loss is the mean over all ranks' volumes (one fp64 all-reduce), and `value` counts the
+voxels of all ranks. D-slab workloads scale strongly: one volume split into D-slabs across the ranks.
+Timing: W untimed warm-up steps,
 then K steps each bracketed by CUDA events on the launching stream, an L2 flush (256 MiB write)
 before every step outside the events, barrier + synchronize around the whole timed region, max over
 ranks. `roofline` times the dominant kernel alone (one C-ABI launch per timing), `e2e` the same public
@@ -136,12 +138,12 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def make_inputs(workload, device):
+def make_inputs(workload, device, seed=0):
     from fused_lncc import synth
     shape, k, dtype, kind = WORKLOADS[workload]
     tdt = torch.float32 if dtype == "fp32" else torch.bfloat16
     if kind == "blurred":
-        pred, target = synth.blurred_pair(shape, device=device, dtype=tdt)
+        pred, target = synth.blurred_pair(shape, seed=seed, device=device, dtype=tdt)
     elif kind == "gigavoxel":
         pred, target = synth.gigavoxel_pair(shape, device=device, dtype=tdt)
     else:
@@ -239,23 +241,31 @@ def main():
     import torch.distributed as dist
     import fused_lncc
     from fused_lncc import _lib
-    from fused_lncc.dist import sharded_lncc_loss, volume_range
+    from fused_lncc.dist import sharded_lncc_loss
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    out_fd = 1
     if world > 1:
+        # NCCL may print to the process's stdout (its version banner, for one); send all of that to
+        # stderr so that stdout carries exactly the one JSON line, written through a saved descriptor
+        sys.stdout.flush()
+        out_fd = os.dup(1)
+        os.dup2(2, 1)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
-    pred, target, k, dtype = make_inputs(args.workload, dev)
+    slabs = args.workload in SLAB_WORKLOADS
+    # slab workloads split one volume, so every rank builds the same one; volume workloads give each
+    # rank a batch of its own (seed 0 on rank 0: the one-GPU inputs)
+    pred, target, k, dtype = make_inputs(args.workload, dev, seed=0 if slabs else 1000 * rank)
     shape = WORKLOADS[args.workload][0]
     n, c = shape[:2]
     nvol = n * c
-    slabs = args.workload in SLAB_WORKLOADS
     input_sha = None
     if rank == 0 and args.workload == "config1":
         input_sha = fused_lncc.synth.sha256_of(pred)
-    m_global = float(nvol) * shape[2] * shape[3] * shape[4]
+    m_global = float(nvol if slabs else world * nvol) * shape[2] * shape[3] * shape[4]
     if slabs:
         # one volume split into D-slabs; each rank keeps its owned planes plus 2r halo planes
         from fused_lncc.dist import SlabPlan, slab_lncc_loss
@@ -274,13 +284,13 @@ def main():
         def loss_fn(p, t):
             return slab_lncc_loss(p, t, plan, k)
     else:
-        b0, b1 = volume_range(nvol, world, rank)
+        b0, b1 = 0, nvol  # this rank's own batch
         vshape = (nvol, 1, *shape[2:])
-        p_loc = pred.reshape(vshape)[b0:b1].contiguous().requires_grad_(True)
-        t_loc = target.reshape(vshape)[b0:b1].contiguous()
+        p_loc = pred.reshape(vshape).contiguous().requires_grad_(True)
+        t_loc = target.reshape(vshape).contiguous()
         z_rng = (0, shape[2])
         vox_local = p_loc.numel()
-        parallelism = f"volumes/{world}"
+        parallelism = f"data-parallel/{world} ({nvol} volumes per rank)"
         if world > 1:
             def loss_fn(p, t):
                 return sharded_lncc_loss(p, t, k, m_global=m_global)
@@ -372,7 +382,9 @@ def main():
     clocks = sampler.summary()
     if args.kernel_only:
         if rank == 0:
-            print(json.dumps({"kernel_only": True, "ms_kernel": result["ms_kernel"], "clocks": clocks}))
+            sys.stdout.flush()
+            os.write(out_fd, (json.dumps({"kernel_only": True, "ms_kernel": result["ms_kernel"],
+                                          "clocks": clocks}) + "\n").encode())
         if world > 1:
             dist.destroy_process_group()
         return 0
@@ -432,9 +444,11 @@ def main():
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": result["ms_step"], "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if slabs else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
             "config": {"workload": args.workload, "shape": list(shape), "kernel_size": k,
                        "input_dtype": dtype, "volumes_per_rank": b1 - b0,
+                       "global_batch": nvol if slabs else world * nvol,
                        "parallelism": parallelism, "l2": "flushed (256 MiB write) before every step",
                        "input_sha256": input_sha},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -452,7 +466,8 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        sys.stdout.flush()
+        os.write(out_fd, (json.dumps(line) + "\n").encode())
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
