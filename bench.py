@@ -6,7 +6,9 @@
 Prints ONE JSON line on rank 0. A step is one forward + backward of the loss through the public API.
 Volume workloads scale weakly: every rank owns a full batch of the workload's N*C volumes (its own
 seed), the loss is the mean over all ranks' volumes (one fp64 all-reduce), and `value` counts the
-voxels of all ranks. D-slab workloads scale strongly: one volume split into D-slabs across the ranks.
+voxels of all ranks. At N > 1 the line also carries `strong_scaling`: the same step over the one
+batch split across the ranks (the workload's volume sharding), timed the same way. D-slab workloads
+scale strongly: one volume split into D-slabs across the ranks.
 Timing: W untimed warm-up steps,
 then K steps each bracketed by CUDA events on the launching stream, an L2 flush (256 MiB write)
 before every step outside the events, barrier + synchronize around the whole timed region, max over
@@ -241,7 +243,7 @@ def main():
     import torch.distributed as dist
     import fused_lncc
     from fused_lncc import _lib
-    from fused_lncc.dist import sharded_lncc_loss
+    from fused_lncc.dist import sharded_lncc_loss, volume_range
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -361,6 +363,39 @@ def main():
             torch.cuda.synchronize(dev)
             ms_step = sum(s.elapsed_time(e) for s, e in evs) / len(evs)
             result["ms_step"] = max_over_ranks(ms_step)
+            if world > 1 and not slabs:
+                # the BASELINE sharding as well: the one headline batch split across the ranks
+                # (strong scaling), this rank's share of its volumes, loss over the batch
+                sb0, sb1 = volume_range(nvol, world, rank)
+                p_s = p_loc.detach()[sb0:sb1].clone().requires_grad_(True)
+                t_s = t_loc[sb0:sb1].contiguous()
+                m_strong = float(nvol) * shape[2] * shape[3] * shape[4]
+
+                def step_strong():
+                    p_s.grad = None
+                    sharded_lncc_loss(p_s, t_s, k, m_global=m_strong).backward()
+
+                for _ in range(args.warmup):
+                    step_strong()
+                torch.cuda.synchronize(dev)
+                barrier()
+                torch.cuda.synchronize(dev)
+                sev = []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record(stream)
+                    step_strong()
+                    e.record(stream)
+                    sev.append((s, e))
+                torch.cuda.synchronize(dev)
+                barrier()
+                torch.cuda.synchronize(dev)
+                ms_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in sev) / len(sev))
+                result["strong"] = {"value": m_strong / (ms_s * 1e-3) / 1e9, "unit": "Gvoxel/s",
+                                    "ms_per_step": ms_s, "volumes_per_rank": sb1 - sb0,
+                                    "global_batch": nvol}
+                del p_s, t_s
         # ---- roofline: the dominant kernel alone -----------------------------------------------------
         for _ in range(args.warmup):
             kernel_launch()
@@ -466,6 +501,8 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if "strong" in result:
+            line["strong_scaling"] = result["strong"]
         sys.stdout.flush()
         os.write(out_fd, (json.dumps(line) + "\n").encode())
     if world > 1:
