@@ -84,7 +84,7 @@ template <int R>
 struct Smem {
   float dw[2][Geo<R>::ER][5][SPAN];  // W-boxed D sums (Sp, St, Spp, Stt, 2*Spt) per row, chunk-swizzled
   float ah[2][3][TY][SPAN];          // H-boxed adjoints (a, b, c) of the CTA's own rows
-  unsigned long long bar[8];         // dw_full[2], dw_empty[2], ah_full[2], ah_empty[2]
+  unsigned long long bar[16];        // dw_full[2], dw_empty[2], ah_full[2], ah_empty[2], xd[4], ya[4]
   double red[8];                     // BC warps' loss partials
   uint32_t tmem_base;
   int abort_flag;
@@ -96,7 +96,7 @@ constexpr int smem_bytes() { return int((sizeof(Smem<R>) + 1023) / 1024 * 1024);
 static_assert(smem_bytes<1>() > 116 * 1024, "ws smem: one CTA per SM");
 static_assert(smem_bytes<4>() <= 227 * 1024, "ws smem: 227 KB per CTA");
 
-enum { BAR_DW_FULL = 0, BAR_DW_EMPTY = 2, BAR_AH_FULL = 4, BAR_AH_EMPTY = 6 };
+enum { BAR_DW_FULL = 0, BAR_DW_EMPTY = 2, BAR_AH_FULL = 4, BAR_AH_EMPTY = 6, BAR_XD = 8, BAR_YA = 12 };
 
 // Physical float offset of logical column x in a 128-float row. The 16-byte chunks of each 128-byte
 // group are permuted (chunk ^= group & 3) so that the eight lanes of a row in the row layout, whose
@@ -416,7 +416,7 @@ struct Seg {
 template <int R, typename S, bool GRAD, int CW>
 __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   constexpr int NCH = VW / CW;  // global-memory chunks per lane
-  constexpr int K = Geo<R>::K, ER = Geo<R>::ER;
+  constexpr int K = Geo<R>::K;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   using SM = Smem<R>;
   SM& sm = *reinterpret_cast<SM*>(smem_raw);
@@ -443,6 +443,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       mbar_init(bar(BAR_AH_FULL, i), 8);   // BC warps
       mbar_init(bar(BAR_AH_EMPTY, i), 4);  // D warps
     }
+    for (int w = 0; w < 4; ++w) {  // per pair (A warp w, D warp 12 + w), which share TMEM lanes and rows
+      mbar_init(bar(BAR_XD, w), 1);  // D warp: its fields of the step's DW rows are written
+      mbar_init(bar(BAR_YA, w), 1);  // A warp: the step's running sums are in TMEM
+    }
     sm.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -462,6 +466,11 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   cluster.sync();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
+  // With the running D sums of the D group in TMEM (k <= 7), the D group also boxes fields 3 and 4
+  // (Stt, 2*Spt) of the A group's sums along W: A's W box is on the loop that bounds a step (A writes
+  // plane s+2 once the column groups release plane s), the D group idles while the column groups sweep.
+  constexpr bool DASSIST = Geo<R>::DSUM_TMEM;
+  constexpr int NFA = DASSIST ? 3 : 5;  // fields the A group boxes
   const float nf = a.n, nh = 0.5f * a.n, ndr = a.n * a.dr;
   double acc = 0.0;  // BC: loss partial
   // After a timed-out wait (a protocol error) every warp leaves its loops (warp-uniformly) without
@@ -492,6 +501,43 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
     const int c0 = sg.zs - R;
     const S* __restrict__ P = reinterpret_cast<const S*>(a.p) + sg.b * D * HW;
     const S* __restrict__ T = reinterpret_cast<const S*>(a.t) + sg.b * D * HW;
+
+    // D warp's share of the W box of step st (fields 3 and 4 of the paired A warp's sums, same TMEM
+    // lanes, same DW rows), once the buffer is free and the sums are complete; false after an abort.
+    auto d_part = [&](uint32_t st, bool valid) -> bool {
+      const int i = int(st & 1u);
+      const int wq = warp & 3;
+      mbar_wait(bar(BAR_DW_EMPTY, i), ((st >> 1) & 1u) ^ 1u, abort_flag);
+      mbar_wait(bar(BAR_YA, wq), st & 1u, abort_flag);
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (valid) {
+        const int yl = wq * 4 + (lane >> 3), q = lane & 7;
+        const uint32_t tmA = sm.tmem_base + (uint32_t(32 * wq) << 16) + Geo<R>::TM_A;
+        const uint32_t own = smem_addr(&sm.dw[i][2 * R + yl][0][0]);
+        uint32_t choff[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) choff[j] = uint32_t(swz_chunk(4 * q + j) * 4);
+        uint32_t ub[2][16];
+        tm_ld16_issue(tmA + uint32_t(16 * 3), ub[0]);
+        tm_wait_ld16(ub[0]);
+#pragma unroll
+        for (int f = 3; f < 5; ++f) {
+          if (f == 3) tm_ld16_issue(tmA + uint32_t(16 * 4), ub[1]);
+          float v[16];
+#pragma unroll
+          for (int m = 0; m < 16; ++m) v[m] = __uint_as_float(ub[f - 3][m]);
+          wbox16<R>(v, q, [&](int j, float4 w4) { sts4(own + uint32_t(f * SPAN * 4) + choff[j], w4); });
+          if (f == 3) tm_wait_ld16(ub[1]);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // for the halo bulk copy
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(bar(BAR_XD, wq));
+      return true;
+    };
+    auto plane_ok = [&](int it) { return c0 + it >= 0 && c0 + it < D; };
 
     if (role == 0) {
       // ===================================== A =========================================================
@@ -586,6 +632,16 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         load_raw(c0 + R < D, c0 + R, false, 0, r);
         dsum_update(r);
       }
+      // the sums of a step are complete: the paired D warp may box its fields
+      auto sums_ready = [&]() {
+        if constexpr (DASSIST) {
+          tm_wait_st();
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cta(bar(BAR_YA, warp));
+        }
+      };
+      sums_ready();
       // halo rows sent to the neighbours by bulk copy, per field: my first 2R rows go to the CTA above
       // (its rows [TY + 2R, TY + 4R)), my last 2R rows to the CTA below (its rows [0, 2R))
       constexpr uint32_t kHaloBytes = 2 * R * 5 * SPAN * 4;  // 2R rows x 5 fields
@@ -613,18 +669,25 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           tm_ld16_issue(tmA, ub[0]);
           tm_wait_ld16(ub[0]);
 #pragma unroll
-          for (int f = 0; f < 5; ++f) {
-            if (f + 1 < 5) tm_ld16_issue(tmA + uint32_t(16 * (f + 1)), ub[(f + 1) & 1]);
+          for (int f = 0; f < NFA; ++f) {
+            if (f + 1 < NFA) tm_ld16_issue(tmA + uint32_t(16 * (f + 1)), ub[(f + 1) & 1]);
             float v[16];
 #pragma unroll
             for (int m = 0; m < 16; ++m) v[m] = __uint_as_float(ub[f & 1][m]);
             wbox16<R>(v, q, [&](int j, float4 w4) { sts4(own + uint32_t(f * SPAN * 4) + choff[j], w4); });
-            if (f + 1 < 5) tm_wait_ld16(ub[(f + 1) & 1]);
+            if (f + 1 < NFA) tm_wait_ld16(ub[(f + 1) & 1]);
           }
         }
         // make this warp's rows visible to the bulk-copy (async) proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
+        if constexpr (DASSIST) {  // the paired D warp's fields of these rows
+          mbar_wait(bar(BAR_XD, warp), s & 1u, abort_flag);
+          if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+            a_aborted = true;
+            break;
+          }
+        }
         if (lane == 0) {
           // warp 0 also announces the halo bytes the neighbours send into this CTA for this step
           if (warp == 0) mbar_arrive_expect_tx(bar(BAR_DW_FULL, i), rx_bytes);
@@ -657,7 +720,12 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           reg_fence(r.po[j]);
           reg_fence(r.to[j]);
         }
-        if (more) dsum_update(r);
+        if (more) {
+          // the D warp has read this step's fields 3 and 4 (its arrival came after its TMEM loads)
+          if constexpr (DASSIST) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          dsum_update(r);
+          sums_ready();
+        }
       }
     } else if (role == 1 || role == 2) {
       // ===================================== BC ========================================================
@@ -823,7 +891,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       if constexpr (Geo<R>::DSUM_TMEM) {
         // running sums in TMEM; p, t of the output plane are loaded at the start of the step
         const uint32_t tsum = tm + Geo<R>::TM_DSUM;
+        // the W-box share of the segment's first two steps, then of step s + 2 before step s's adjoints
+        if (!d_part(s, plane_ok(0)) || !d_part(s + 1, plane_ok(1))) break;
         for (int it = 0; it < nsteps; ++it, ++s) {
+          if (it + 2 < nsteps && !d_part(s + 2, plane_ok(it + 2))) break;
           const int c = c0 + it;
           const bool cvalid = c >= 0 && c < D;
           const int o = c - R;
@@ -965,7 +1036,14 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         }
       }
     } else {
-      s += uint32_t(nsteps);  // loss-only: the D group has no work
+      // loss only: the D group's work is its share of the W box
+      if constexpr (DASSIST) {
+        if (!d_part(s, plane_ok(0)) || !d_part(s + 1, plane_ok(1))) break;
+        for (int it = 0; it < nsteps; ++it, ++s)
+          if (it + 2 < nsteps && !d_part(s + 2, plane_ok(it + 2))) break;
+      } else {
+        s += uint32_t(nsteps);
+      }
     }
   }
 

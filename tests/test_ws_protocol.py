@@ -2,7 +2,11 @@
 
 One cluster of CTAs; per CTA 4 A warps, 8 BC warps and 4 D warps walk the same step sequence with random
 work times, and the halo bulk copies (one per A warp: warps 0-1 to the CTA above, 2-3 below) land after
-random delays. Barriers are modelled like mbarriers
+random delays. Each D warp also boxes two of the five fields for its paired A warp (same rows): it
+waits until the buffer is free and the pair's running sums are complete (ya), writes its fields and
+signals xd, which the A warp waits for before announcing its rows and sending the halo; the D warps do
+this for the first two steps of a segment, then for step s + 2 before the adjoints of step s.
+Barriers are modelled like mbarriers
 (arrival count, pending count, transaction bytes, phase). Every arrival and every completed copy is
 tagged with the phase it is meant for; a tag different from the barrier's current phase is a protocol
 violation (the hardware would count it silently in the wrong phase), and actors left waiting at the end
@@ -29,9 +33,11 @@ class Bar:
             self.pending = self.count
 
 
-def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
+def simulate(ncta, steps_valid, always_send, seed, slow_cta=None, seg_len=None):
     rnd = random.Random(seed)
     nsteps = len(steps_valid)
+    seg_len = seg_len or nsteps
+    seg_start = [s - s % seg_len for s in range(nsteps)]  # first step of each step's segment
     bars = {}
     for j in range(ncta):
         nb = 8 * (1 + (j > 0) + (j < ncta - 1))
@@ -40,6 +46,9 @@ def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
             bars[(j, "empty", i)] = Bar(nb)
             bars[(j, "ahfull", i)] = Bar(8)
             bars[(j, "ahempty", i)] = Bar(4)
+        for w in range(4):
+            bars[(j, "xd", w)] = Bar(1)
+            bars[(j, "ya", w)] = Bar(1)
     violations = []
     t = [0.0]
     events = []  # (time, seq, fn)
@@ -79,9 +88,13 @@ def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
     def A(j, w):
         for s in range(nsteps):
             i, u = s & 1, s >> 1
+            if s == seg_start[s]:  # warm-up of the segment's running sums
+                yield ("work", dur(j))
+                arrive((j, "ya", w), s)
             if s >= 2:
                 yield ("wait", (j, "empty", i), u - 1)
             yield ("work", dur(j))
+            yield ("wait", (j, "xd", w), s)
             valid = steps_valid[s]
             send = always_send or valid
             ntx = HALO * ((j > 0) + (j < ncta - 1))
@@ -90,6 +103,9 @@ def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
             nb = j - 1 if w < 2 else j + 1
             if send and 0 <= nb < ncta:
                 at(t[0] + rnd.expovariate(0.5), lambda nb=nb, i=i, u=u: complete_tx((nb, "full", i), u, HALO // 2))
+            if s + 1 < nsteps and seg_start[s + 1] == seg_start[s]:
+                yield ("work", dur(j) * 0.5)  # running sums of the next step
+                arrive((j, "ya", w), s + 1)
 
     def BC(j, w):
         for s in range(nsteps):
@@ -103,9 +119,21 @@ def simulate(ncta, steps_valid, always_send, seed, slow_cta=None):
                     arrive((nb, "empty", i), u)
             arrive((j, "ahfull", i), u)
 
+    def d_part(j, w, st):
+        if st >= 2:
+            yield ("wait", (j, "empty", st & 1), (st >> 1) - 1)
+        yield ("wait", (j, "ya", w), st)
+        yield ("work", dur(j) * 0.3)
+        arrive((j, "xd", w), st)
+
     def D(j, w):
         for s in range(nsteps):
             i, u = s & 1, s >> 1
+            if s == seg_start[s]:
+                for st in (s, s + 1):
+                    yield from d_part(j, w, st)
+            if s + 2 < nsteps and seg_start[s + 2] == seg_start[s]:
+                yield from d_part(j, w, s + 2)
             yield ("wait", (j, "ahfull", i), u)
             yield ("work", dur(j))
             arrive((j, "ahempty", i), u)
@@ -150,7 +178,7 @@ def _steps(R, nseg=3, inner=12):
 def test_protocol_has_no_misaligned_arrivals_or_deadlock():
     for R in (1, 4):
         for seed in range(24):
-            violations, waiting = simulate(8, _steps(R), True, seed, slow_cta=seed % 8)
+            violations, waiting = simulate(8, _steps(R), True, seed, slow_cta=seed % 8, seg_len=12 + 2 * R)
             assert not violations, (R, seed, violations[:3])
             assert waiting == 0, (R, seed)
 
