@@ -10,10 +10,11 @@
 //   A   (warps 0-3)  thread <-> one row, 16 columns. Keeps D running sums of p, t, p*p, t*t, 2*p*t in
 //                    tensor memory (TMEM), updated with the raw plane entering and the one leaving the
 //                    window (both loaded one step ahead), boxes them along W with warp shuffles and
-//                    stores them (DW) for the step's stat plane. The CTA's first and last 2r rows are
-//                    then sent to the neighbouring CTAs' halo rows by bulk copies (TMA engine, one per
-//                    warp and neighbour, completion counted in bytes on the receiver's barrier), so no
-//                    CTA recomputes another CTA's rows.
+//                    stores them (DW) for the step's stat plane (for k <= 7 fields 0-2 only; the D
+//                    warp with the same TMEM lanes and rows boxes fields 3-4). The CTA's first and last
+//                    2r rows are then sent to the neighbouring CTAs' halo rows by bulk copies (TMA
+//                    engine, one per warp and neighbour, completion counted in bytes on the receiver's
+//                    barrier), so no CTA recomputes another CTA's rows.
 //   BC  (warps 4-11) two threads per column, each for half of the CTA's rows: H box of DW over
 //                    8 + 4r rows -> the five window sums -> cc (loss partial) and the three adjoint
 //                    fields on 8 + 2r rows -> H box of the adjoints -> AH for its 8 rows.
@@ -22,7 +23,8 @@
 //                    c - r.
 // DW and AH are double-buffered by step parity. mbarriers per buffer: dw_full (this CTA's A warps have
 // written and the neighbours' halo bytes have landed), dw_empty (BC of this CTA and of both
-// neighbours have read), ah_full, ah_empty. Every wait is bounded: after
+// neighbours have read), ah_full, ah_empty; per pair of A warp w and D warp 12 + w: ya (the step's
+// running sums are in TMEM) and xd (the D warp's fields are written). Every wait is bounded: after
 // kWaitLimitNs the CTA sets an abort flag, every role of the CTA leaves its loops without arriving
 // on a barrier again, and the CTA's loss partial becomes NaN.
 //
