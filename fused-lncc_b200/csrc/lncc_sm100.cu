@@ -470,6 +470,7 @@ static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
 // band kernel host side
 // ------------------------------------------------------------------------------------------------
 static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band, 3 warp-specialised
+static std::atomic<int> g_companion{1};      // warp-specialised kernel: companion launch on idle SMs
 
 // Row segments per column in the band kernel's column phases (threads = 128 * segments).
 // LNCC_BAND_SEGMENTS=2|4 overrides the default (a tuning knob; both variants compute the same).
@@ -726,11 +727,19 @@ struct WsPlan {
   int64_t nclusters;
   int64_t ipc;
   const void* fn;
+  // Companion launch on the SMs the main launch leaves idle (clusters of 8 at one CTA per SM do not
+  // tile every GPC): clusters of kCompanionCy CTAs over the last `b2` volumes, run concurrently on a
+  // second stream. b2 == 0: none.
+  int64_t b2;
+  int tiles_y2;
+  int64_t total2, nclusters2, ipc2;
+  int64_t parts() const { return int64_t(cy) * nclusters + int64_t(kCompanionCy) * nclusters2; }
+  static constexpr int kCompanionCy = 2;
 };
 
 static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bool grad, int64_t z_begin,
                            int64_t z_end, const void* p, const void* t, const void* g) {
-  WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr};
+  WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr, 0, 0, 0, 0, 0};
   const int choice = g_kernel_choice.load();
   if (choice == 1 || choice == 2) return wp;
   // pointers unknown (workspace query): plan as for aligned tensors
@@ -750,13 +759,42 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   const int ty = ws::tile_count(int(H), span_y, R, 1);
   const int maxc = ws_max_clusters(fn, cy, R);
   if (maxc < 1) return wp;
-  const int64_t total = B * int64_t(tx) * ty * (z_end - z_begin);
+  const int64_t dz = z_end - z_begin;
   const int64_t min_ipc = 32;
+  // Companion: when the main launch fills every cluster slot but leaves SMs idle, give the last b2
+  // volumes to clusters of 2 CTAs on those SMs. Their span is 32 rows, so a plane costs ty2 tiles
+  // instead of ty; b2 balances the two launches' cluster-steps (nc / tiles per volume each).
+  int64_t b2 = 0, nc2 = 0;
+  int ty2 = 0;
+  if (cy >= 4 && B >= 2 && B * int64_t(tx) * ty * dz >= min_ipc * maxc && g_companion.load()) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
+      nc2 = (sms - int64_t(cy) * maxc) / WsPlan::kCompanionCy;
+      const int maxc2 = ws_max_clusters(fn, WsPlan::kCompanionCy, R);
+      if (nc2 > maxc2) nc2 = maxc2;
+      if (nc2 >= 2) {
+        ty2 = ws::tile_count(int(H), ws::TY * WsPlan::kCompanionCy, R, 1);
+        const double r1 = double(maxc) / ty, r2 = double(nc2) / ty2;
+        b2 = int64_t(double(B) * r2 / (r1 + r2) + 0.5);
+        if (b2 > B - 1) b2 = B - 1;
+      }
+    }
+    cudaGetLastError();
+  }
+  const int64_t total = (B - b2) * int64_t(tx) * ty * dz;
   int64_t nc = (total + min_ipc - 1) / min_ipc;
   if (nc > maxc) nc = maxc;
   if (nc < 1) nc = 1;
   const int64_t ipc = (total + nc - 1) / nc;
   nc = (total + ipc - 1) / ipc;
+  if (b2 > 0) {
+    wp.b2 = b2;
+    wp.tiles_y2 = ty2;
+    wp.total2 = b2 * int64_t(tx) * ty2 * dz;
+    wp.ipc2 = (wp.total2 + nc2 - 1) / nc2;
+    wp.nclusters2 = (wp.total2 + wp.ipc2 - 1) / wp.ipc2;
+  }
   wp.ok = true;
   wp.cy = cy;
   wp.tiles_x = tx;
@@ -768,21 +806,103 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   return wp;
 }
 
-static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t st) {
+static cudaError_t launch_ws_grid(const WsPlan& wp, int cy, int64_t nclusters, const ws::Args& wa,
+                                  cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(wp.cy);
+  attr[0].val.clusterDim.x = unsigned(cy);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(unsigned(wp.cy), unsigned(wp.nclusters), 1);
+  cfg.gridDim = dim3(unsigned(cy), unsigned(nclusters), 1);
   cfg.blockDim = dim3(ws::NT, 1, 1);
   cfg.dynamicSmemBytes = size_t(ws_smem_for(wp.R));
   cfg.stream = st;
   void* args[] = {const_cast<ws::Args*>(&wa)};
   return cudaLaunchKernelExC(&cfg, wp.fn, args);
+}
+
+// Per-device stream for the companion launch, and per-thread fork / join events (no timing), made on
+// first use outside stream capture and kept for the life of the process. Returns false when they
+// cannot be had, in which case the caller runs the main launch over every volume.
+static bool companion_resources(int dev, bool create, cudaStream_t* comp, cudaEvent_t* fork,
+                                cudaEvent_t* join) {
+  static std::mutex mu;
+  static cudaStream_t streams[64] = {nullptr};
+  thread_local cudaEvent_t ev[64][2] = {};
+  if (dev < 0 || dev >= 64) return false;
+  if (!ev[dev][0]) {
+    if (!create) return false;
+    if (cudaEventCreateWithFlags(&ev[dev][0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev[dev][1], cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      ev[dev][0] = ev[dev][1] = nullptr;
+      return false;
+    }
+  }
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!streams[dev] && !create) return false;
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      streams[dev] = nullptr;
+      return false;
+    }
+    *comp = streams[dev];
+  }
+  *fork = ev[dev][0];
+  *join = ev[dev][1];
+  return true;
+}
+
+// Main launch on `st`; with a companion, the companion launch runs on the library's second stream,
+// forked from and joined back into `st` (both legal under stream capture), so work queued on `st`
+// after this call sees both. *nparts: the loss partials written, at wa.partials.
+static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t st, int64_t B, int64_t D,
+                             int64_t H, int64_t W, int dtype, int64_t* nparts) {
+  cudaStream_t comp = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool use2 = wp.b2 > 0;
+  if (use2) {
+    // under stream capture only resources made earlier are used (no creation while capturing)
+    int dev = 0;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    use2 = cudaGetDevice(&dev) == cudaSuccess && cudaStreamIsCapturing(st, &cs) == cudaSuccess &&
+           companion_resources(dev, cs == cudaStreamCaptureStatusNone, &comp, &fork, &join);
+    cudaGetLastError();
+  }
+  if (!use2) {
+    // every volume in the main launch, over the same number of clusters (so the same partials)
+    ws::Args a1 = wa;
+    a1.total_items = B * int64_t(wp.tiles_x) * wp.tiles_y * (int64_t(wa.z_end) - wa.z_begin);
+    a1.items_per_cluster = (a1.total_items + wp.nclusters - 1) / wp.nclusters;
+    const int64_t nc = (a1.total_items + a1.items_per_cluster - 1) / a1.items_per_cluster;
+    *nparts = int64_t(wp.cy) * nc;
+    return launch_ws_grid(wp, wp.cy, nc, a1, st);
+  }
+  *nparts = wp.parts();
+  cudaError_t e = cudaEventRecord(fork, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, fork, 0);
+  if (e == cudaSuccess) e = launch_ws_grid(wp, wp.cy, wp.nclusters, wa, st);
+  if (e == cudaSuccess) {
+    const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+    const int64_t b1 = B - wp.b2;
+    ws::Args a2 = wa;
+    a2.p = static_cast<const char*>(wa.p) + size_t(b1 * D * H * W) * esz;
+    a2.t = static_cast<const char*>(wa.t) + size_t(b1 * D * H * W) * esz;
+    if (wa.g) a2.g = static_cast<char*>(wa.g) + size_t(b1 * (int64_t(wa.z_end) - wa.z_begin) * H * W) * esz;
+    a2.partials = wa.partials + int64_t(wp.cy) * wp.nclusters;
+    a2.tiles_y = wp.tiles_y2;
+    a2.span_y = ws::TY * WsPlan::kCompanionCy;
+    a2.total_items = wp.total2;
+    a2.items_per_cluster = wp.ipc2;
+    e = launch_ws_grid(wp, WsPlan::kCompanionCy, wp.nclusters2, a2, comp);
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(join, comp);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, join, 0);
+  return e;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -876,8 +996,7 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
   size_t need = size_t(pl.nblocks) * sizeof(double);
   for (int gflag = 0; gflag < 2; ++gflag) {
     const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, gflag != 0, z_begin, z_end, nullptr, nullptr, nullptr);
-    if (wp.ok && size_t(wp.cy) * size_t(wp.nclusters) * sizeof(double) > need)
-      need = size_t(wp.cy) * size_t(wp.nclusters) * sizeof(double);
+    if (wp.ok && size_t(wp.parts()) * sizeof(double) > need) need = size_t(wp.parts()) * sizeof(double);
   }
   const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, true, z_begin, z_end, nullptr, nullptr, nullptr);
   if (bp.ok) {
@@ -909,7 +1028,7 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
   const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
   BandPlan bp{false, kernel_size / 2, 0, 0, 0, nullptr};
   if (!wp.ok) bp = make_band_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
-  const int64_t nparts = wp.ok ? int64_t(wp.cy) * wp.nclusters : bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
+  int64_t nparts = wp.ok ? wp.parts() : bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
   const size_t need = size_t(nparts) * sizeof(double);
   if (!workspace || workspace_bytes < need || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
   if (loss_out && !(loss_count > 0.0)) return LNCC_ERR_BAD_ARG;
@@ -961,7 +1080,7 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     wa.span_y = ws::TY * wp.cy;
     wa.total_items = wp.total;
     wa.items_per_cluster = wp.ipc;
-    e = launch_ws(wp, wa, stream);
+    e = launch_ws(wp, wa, stream, B, D, H, W, dtype, &nparts);
   } else if (bp.ok) {
     band::BandArgs ba;
     ba.p = pred;
@@ -1016,6 +1135,8 @@ int lncc_select_kernel(int which) {
   g_kernel_choice.store(which);
   return LNCC_OK;
 }
+
+int lncc_set_companion(int enable) { return g_companion.exchange(enable ? 1 : 0); }
 
 int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                       int64_t W, int kernel_size, float smooth_dr, float* ncc, float* A, float* Bc, float* Cc,

@@ -36,6 +36,7 @@ SIGNATURES = {
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "lncc_set_companion": (ctypes.c_int, [ctypes.c_int]),
     "lncc_fused_forward_noalloc": (ctypes.c_int, [
         _vp, _vp, ctypes.c_int,                      # pred, target, dtype
         _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
@@ -108,3 +109,10 @@ def select_kernel(which):
     band kernel, else the general sweep kernel), 1 general sweep kernel, 2 band kernel where supported,
     3 warp-specialised cluster kernel where supported."""
     check(load().lncc_select_kernel(int(which)), "lncc_select_kernel")
+
+
+def set_companion(enable):
+    """Process-wide switch of the warp-specialised kernel's companion launch (clusters of 2 CTAs on
+    the SMs that clusters of 8 leave idle, for the last volumes of a call); returns the previous
+    setting."""
+    return bool(load().lncc_set_companion(1 if enable else 0))

@@ -156,6 +156,15 @@ int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_
  */
 int lncc_select_kernel(int which);
 
+/*
+ * Companion launch of the warp-specialised kernel (default on): clusters of 8 CTAs at one CTA per SM
+ * do not tile every GPC of a B200 (15 clusters = 120 of 148 SMs), so when a call has enough volumes
+ * the last few go to clusters of 2 CTAs on the idle SMs, run concurrently on a library-owned stream
+ * that is forked from and joined back into the caller's stream. 0 turns it off for the process.
+ * Returns the previous setting. No counterpart in the reference.
+ */
+int lncc_set_companion(int enable);
+
 #ifdef __cplusplus
 }
 #endif

@@ -354,6 +354,55 @@ def test_ws_repeat_bitwise():
         _lib.select_kernel(_lib.KERNEL_AUTO)
 
 
+# Companion launch: in a call with enough volumes the last ones run in clusters of 2 CTAs on the SMs
+# that clusters of 8 leave idle, concurrently on a second stream. The result must not depend on it.
+@pytest.mark.parametrize("shape,k,dtype", [((1, 8, 64, 128, 128), 7, torch.float32),
+                                           ((3, 3, 64, 128, 128), 5, torch.float32),
+                                           ((2, 8, 48, 128, 136), 9, torch.bfloat16)])
+def test_ws_companion_matches_single_launch(shape, k, dtype):
+    from fused_lncc import _lib, synth
+    pred, target = synth.blurred_pair(shape, device="cuda", dtype=dtype)
+    outs = []
+    for on in (True, False):
+        prev = _lib.set_companion(on)
+        try:
+            s = torch.zeros((), dtype=torch.float64, device="cuda")
+            _, g = lncc_fused(pred, target, k, grad_scale=1.0, cc_sum_out=s)
+            torch.cuda.synchronize()
+            outs.append((s.item(), g.float()))
+        finally:
+            _lib.set_companion(prev)
+    (s1, g1), (s2, g2) = outs
+    # the companion ran: it computes the last volume on its own row tiling, so that volume's gradient
+    # differs in the last bits (the kernel is deterministic: one plan gives identical bits)
+    assert not torch.equal(g1.reshape(-1, *shape[2:])[-1], g2.reshape(-1, *shape[2:])[-1])
+    assert abs(s1 - s2) < 1e-6 * max(1.0, abs(s1)), (s1, s2)
+    cos, rel = cos_rel(g1, g2)
+    assert cos > 0.99999 and rel < (1e-5 if dtype == torch.float32 else 5e-3), (cos, rel)
+
+
+def test_ws_companion_under_graph_capture():
+    """The fork to the companion's stream and the join are captured like any stream work: a replay
+    gives the eager result bit for bit (the stream and events were made by the eager call)."""
+    from fused_lncc import synth
+    pred, target = synth.blurred_pair((1, 8, 64, 128, 128), device="cuda")
+    s_e = torch.zeros((), dtype=torch.float64, device="cuda")
+    _, g_e = lncc_fused(pred, target, 7, cc_sum_out=s_e)
+    s = torch.zeros_like(s_e)
+    g = torch.empty_like(g_e)
+    lncc_fused(pred, target, 7, cc_sum_out=s, out=g)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        lncc_fused(pred, target, 7, cc_sum_out=s, out=g)
+    s.zero_()
+    g.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert s.item() == s_e.item() and torch.equal(g, g_e)
+    del graph
+
+
 def test_band_bf16_and_loss_only():
     from fused_lncc import synth
     pred, target = synth.blurred_pair((2, 2, 40, 64, 64), device="cuda", dtype=torch.bfloat16)
