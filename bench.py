@@ -474,6 +474,7 @@ def main():
         # which kernel the library picks for this shape (automatic choice, include/lncc.h): the
         # warp-specialised cluster kernel whenever W % 4 == 0 (torch allocations are aligned)
         kname = "lncc_ws_kernel" if W % 4 == 0 else "lncc_sweep_kernel"
+        launches_per_call = lib.lncc_launch_count(nb, D, H, W, k, dtc, z_rng[0], z_rng[1], 1)
         traffic = profile_traffic(kname, args.workload) if world == 1 else None
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
@@ -489,13 +490,15 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
                          "traffic": traffic, "kernel": kname,
-                         "algorithmic_bytes_per_voxel": bpv, "ms_per_launch": result["ms_kernel"]},
+                         "algorithmic_bytes_per_voxel": bpv, "ms_per_launch": result["ms_kernel"],
+                         "launches_per_call": launches_per_call},
             "e2e": {"value": vox_global / (ms_e2e * 1e-3) / 1e9, "unit": "Gvoxel/s",
                     "h2d_bytes_per_step": 2 * p_host.numel() * esz, "d2h_bytes_per_step": 4,
                     "ms_per_step": ms_e2e},
-            # fused kernel + loss reduction per compute call (3 calls per slab step when halos are
-            # exchanged, to overlap the interior), plus the grad_out scale kernel
-            "gpu_launches": (2 * (3 if slabs and world > 1 else 1) + 1) * args.steps,
+            # per compute call the fused kernel (plus its companion launch on idle SMs when the
+            # library plans one) and the loss reduction, 3 calls per slab step when halos are
+            # exchanged (to overlap the interior); plus the grad_out scale kernel
+            "gpu_launches": ((launches_per_call + 1) * (3 if slabs and world > 1 else 1) + 1) * args.steps,
             "clocks": clocks,
             "loss": loss_val,
         }

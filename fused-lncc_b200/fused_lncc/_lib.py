@@ -37,6 +37,8 @@ SIGNATURES = {
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
     "lncc_set_companion": (ctypes.c_int, [ctypes.c_int]),
+    "lncc_launch_count": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int, _c_i64,
+                                         _c_i64, ctypes.c_int]),
     "lncc_fused_forward_noalloc": (ctypes.c_int, [
         _vp, _vp, ctypes.c_int,                      # pred, target, dtype
         _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W

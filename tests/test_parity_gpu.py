@@ -362,10 +362,14 @@ def test_ws_repeat_bitwise():
 def test_ws_companion_matches_single_launch(shape, k, dtype):
     from fused_lncc import _lib, synth
     pred, target = synth.blurred_pair(shape, device="cuda", dtype=dtype)
+    lib = _lib.load()
+    B, (D, H, W) = shape[0] * shape[1], shape[2:]
+    dt = 0 if dtype == torch.float32 else 1
     outs = []
     for on in (True, False):
         prev = _lib.set_companion(on)
         try:
+            assert lib.lncc_launch_count(B, D, H, W, k, dt, 0, D, 1) == (2 if on else 1)
             s = torch.zeros((), dtype=torch.float64, device="cuda")
             _, g = lncc_fused(pred, target, k, grad_scale=1.0, cc_sum_out=s)
             torch.cuda.synchronize()
