@@ -626,7 +626,8 @@ static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cud
 // ------------------------------------------------------------------------------------------------
 // warp-specialised cluster kernel host side (lncc_ws.cuh)
 // ------------------------------------------------------------------------------------------------
-constexpr int kWsMaxCluster = 8;  // portable cluster size; taller planes are cut into row tiles
+constexpr int kWsMaxCluster = 8;   // portable cluster size; taller planes are cut into row tiles
+constexpr int kWsMaxTall = 16;     // non-portable cluster size, tried for planes of 129 - 256 rows
 
 // Global-memory chunk width of the kernel for this call: 8 columns (256-bit fp32 / 128-bit bf16
 // accesses) when W % 8 == 0 and the base pointers are aligned to a chunk, else 4 columns when
@@ -652,6 +653,9 @@ static cudaError_t ws_prepare(const void** fn_out) {
   if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
     e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, ws::smem_bytes<R>());
     if (e != cudaSuccess) return e;
+    // clusters of up to 16 CTAs (tall planes); the occupancy query then reports how many fit
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      cudaGetLastError();
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
   *fn_out = reinterpret_cast<const void*>(kfn);
@@ -728,9 +732,10 @@ struct WsPlan {
   int64_t ipc;
   const void* fn;
   // Companion launch on the SMs the main launch leaves idle (clusters of 8 at one CTA per SM do not
-  // tile every GPC): clusters of kCompanionCy CTAs over the last `b2` volumes, run concurrently on a
-  // second stream. b2 == 0: none.
+  // tile every GPC): clusters of kCompanionCy CTAs over the last `b2` volumes, or, for a single
+  // volume, its last `z2` output planes, run concurrently on a second stream. Both 0: none.
   int64_t b2;
+  int64_t z2;
   int tiles_y2;
   int64_t total2, nclusters2, ipc2;
   int64_t parts() const { return int64_t(cy) * nclusters + int64_t(kCompanionCy) * nclusters2; }
@@ -739,7 +744,7 @@ struct WsPlan {
 
 static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bool grad, int64_t z_begin,
                            int64_t z_end, const void* p, const void* t, const void* g) {
-  WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr, 0, 0, 0, 0, 0};
+  WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr, 0, 0, 0, 0, 0, 0};
   const int choice = g_kernel_choice.load();
   if (choice == 1 || choice == 2) return wp;
   // pointers unknown (workspace query): plan as for aligned tensors
@@ -754,19 +759,31 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   const int R = k / 2;
   int cy = int((H + ws::TY - 1) / ws::TY);
   if (cy > kWsMaxCluster) cy = kWsMaxCluster;
-  const int span_y = ws::TY * cy;
+  int ty = ws::tile_count(int(H), ws::TY * cy, R, 1);
   const int tx = ws::tile_count(int(W), ws::SPAN, R, cw);
-  const int ty = ws::tile_count(int(H), span_y, R, 1);
-  const int maxc = ws_max_clusters(fn, cy, R);
+  int maxc = ws_max_clusters(fn, cy, R);
   if (maxc < 1) return wp;
+  // A plane of 129 - 256 rows needs 2 - 3 overlapping row tiles in clusters of 8 but one in a taller
+  // (non-portable) cluster, of which fewer fit: take the taller one when its row tiles per resident
+  // cluster are fewer (every cluster advances one tile-plane per step whatever its height).
+  if (H > int64_t(ws::TY) * kWsMaxCluster && H <= int64_t(ws::TY) * kWsMaxTall) {
+    const int cyt = int((H + ws::TY - 1) / ws::TY);
+    const int maxt = ws_max_clusters(fn, cyt, R);
+    if (maxt >= 1 && 1.0 / maxt < double(ty) / maxc) {
+      cy = cyt;
+      ty = 1;
+      maxc = maxt;
+    }
+  }
   const int64_t dz = z_end - z_begin;
   const int64_t min_ipc = 32;
   // Companion: when the main launch fills every cluster slot but leaves SMs idle, give the last b2
-  // volumes to clusters of 2 CTAs on those SMs. Their span is 32 rows, so a plane costs ty2 tiles
-  // instead of ty; b2 balances the two launches' cluster-steps (nc / tiles per volume each).
-  int64_t b2 = 0, nc2 = 0;
+  // volumes (a single volume: its last z2 planes) to clusters of 2 CTAs on those SMs. Their span is
+  // 32 rows, so a plane costs ty2 tiles instead of ty; the split balances the two launches'
+  // cluster-steps (resident clusters / row tiles per plane each).
+  int64_t b2 = 0, z2 = 0, nc2 = 0;
   int ty2 = 0;
-  if (cy >= 4 && B >= 2 && B * int64_t(tx) * ty * dz >= min_ipc * maxc && g_companion.load()) {
+  if (cy >= 4 && B * int64_t(tx) * ty * dz >= min_ipc * maxc && g_companion.load()) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
@@ -776,22 +793,30 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
       if (nc2 >= 2) {
         ty2 = ws::tile_count(int(H), ws::TY * WsPlan::kCompanionCy, R, 1);
         const double r1 = double(maxc) / ty, r2 = double(nc2) / ty2;
-        b2 = int64_t(double(B) * r2 / (r1 + r2) + 0.5);
-        if (b2 > B - 1) b2 = B - 1;
+        if (B >= 2) {
+          b2 = int64_t(double(B) * r2 / (r1 + r2) + 0.5);
+          if (b2 > B - 1) b2 = B - 1;
+        } else {
+          // planes of one volume: each launch's segments start with a 2r-plane warm-up, so neither
+          // share may be tiny
+          z2 = int64_t(double(dz) * r2 / (r1 + r2) + 0.5);
+          if (z2 < 8 || dz - z2 < 8) z2 = 0;
+        }
       }
     }
     cudaGetLastError();
   }
-  const int64_t total = (B - b2) * int64_t(tx) * ty * dz;
+  const int64_t total = (B - b2) * int64_t(tx) * ty * (dz - z2);
   int64_t nc = (total + min_ipc - 1) / min_ipc;
   if (nc > maxc) nc = maxc;
   if (nc < 1) nc = 1;
   const int64_t ipc = (total + nc - 1) / nc;
   nc = (total + ipc - 1) / ipc;
-  if (b2 > 0) {
+  if (b2 > 0 || z2 > 0) {
     wp.b2 = b2;
+    wp.z2 = z2;
     wp.tiles_y2 = ty2;
-    wp.total2 = b2 * int64_t(tx) * ty2 * dz;
+    wp.total2 = (b2 > 0 ? b2 * dz : z2) * int64_t(tx) * ty2;
     wp.ipc2 = (wp.total2 + nc2 - 1) / nc2;
     wp.nclusters2 = (wp.total2 + wp.ipc2 - 1) / wp.ipc2;
   }
@@ -864,7 +889,7 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
                              int64_t H, int64_t W, int dtype, int64_t* nparts) {
   cudaStream_t comp = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
-  bool use2 = wp.b2 > 0;
+  bool use2 = wp.b2 > 0 || wp.z2 > 0;
   if (use2) {
     // under stream capture only resources made earlier are used (no creation while capturing)
     int dev = 0;
@@ -883,16 +908,23 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
     return launch_ws_grid(wp, wp.cy, nc, a1, st);
   }
   *nparts = wp.parts();
-  cudaError_t e = cudaEventRecord(fork, st);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, fork, 0);
-  if (e == cudaSuccess) e = launch_ws_grid(wp, wp.cy, wp.nclusters, wa, st);
-  if (e == cudaSuccess) {
-    const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  ws::Args a1 = wa, a2 = wa;
+  if (wp.z2 > 0) {  // one volume: the main launch takes planes [z_begin, zs), the companion [zs, z_end)
+    const int zs = wa.z_end - int(wp.z2);
+    a1.z_end = zs;
+    a2.z_begin = zs;
+    if (wa.g) a2.g = static_cast<char*>(wa.g) + size_t(int64_t(zs - wa.z_begin) * H * W) * esz;
+  } else {  // the main launch takes volumes [0, B - b2), the companion the rest
     const int64_t b1 = B - wp.b2;
-    ws::Args a2 = wa;
     a2.p = static_cast<const char*>(wa.p) + size_t(b1 * D * H * W) * esz;
     a2.t = static_cast<const char*>(wa.t) + size_t(b1 * D * H * W) * esz;
     if (wa.g) a2.g = static_cast<char*>(wa.g) + size_t(b1 * (int64_t(wa.z_end) - wa.z_begin) * H * W) * esz;
+  }
+  cudaError_t e = cudaEventRecord(fork, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, fork, 0);
+  if (e == cudaSuccess) e = launch_ws_grid(wp, wp.cy, wp.nclusters, a1, st);
+  if (e == cudaSuccess) {
     a2.partials = wa.partials + int64_t(wp.cy) * wp.nclusters;
     a2.tiles_y = wp.tiles_y2;
     a2.span_y = ws::TY * WsPlan::kCompanionCy;
@@ -1144,7 +1176,7 @@ int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_siz
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
   if (B < 1 || D < 1 || H < 1 || W < 1 || z_begin < 0 || z_end > D || z_end <= z_begin) return LNCC_ERR_BAD_ARG;
   const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != 0, z_begin, z_end, nullptr, nullptr, nullptr);
-  return (wp.ok && wp.b2 > 0) ? 2 : 1;
+  return (wp.ok && (wp.b2 > 0 || wp.z2 > 0)) ? 2 : 1;
 }
 
 int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,

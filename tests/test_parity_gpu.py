@@ -314,7 +314,9 @@ def test_band_equals_sweep_blurred(k):
 # (W % 8 == 0 takes 8-column global accesses, W % 8 == 4 the 4-column ones)
 @pytest.mark.parametrize("shape,k", [((1, 1, 20, 40, 224), 9), ((1, 1, 24, 200, 200), 7), ((1, 1, 33, 130, 16), 5),
                                      ((1, 1, 6, 256, 16), 3), ((1, 1, 3, 2, 4), 7), ((2, 1, 17, 260, 12), 3),
-                                     ((1, 2, 24, 40, 132), 7), ((1, 1, 30, 48, 252), 9)])
+                                     ((1, 2, 24, 40, 132), 7), ((1, 1, 30, 48, 252), 9),
+                                     # 129 - 256 rows: one tile in a cluster of up to 16 CTAs
+                                     ((1, 1, 20, 256, 136), 9), ((1, 2, 12, 250, 64), 7), ((1, 1, 9, 144, 32), 5)])
 def test_ws_tiled_matches_sweep(shape, k):
     from fused_lncc import _lib
     g = torch.Generator().manual_seed(sum(shape) * 7 + k)
@@ -354,11 +356,15 @@ def test_ws_repeat_bitwise():
         _lib.select_kernel(_lib.KERNEL_AUTO)
 
 
-# Companion launch: in a call with enough volumes the last ones run in clusters of 2 CTAs on the SMs
-# that clusters of 8 leave idle, concurrently on a second stream. The result must not depend on it.
+# Companion launch: in a call with enough volumes the last ones (one volume: its last planes) run in
+# clusters of 2 CTAs on the SMs that the main clusters leave idle, concurrently on a second stream. The
+# result must not depend on it.
 @pytest.mark.parametrize("shape,k,dtype", [((1, 8, 64, 128, 128), 7, torch.float32),
                                            ((3, 3, 64, 128, 128), 5, torch.float32),
-                                           ((2, 8, 48, 128, 136), 9, torch.bfloat16)])
+                                           ((2, 8, 48, 128, 136), 9, torch.bfloat16),
+                                           # one volume: the companion takes the last planes
+                                           ((1, 1, 512, 128, 128), 5, torch.float32),
+                                           ((1, 1, 160, 256, 256), 7, torch.float32)])
 def test_ws_companion_matches_single_launch(shape, k, dtype):
     from fused_lncc import _lib, synth
     pred, target = synth.blurred_pair(shape, device="cuda", dtype=dtype)
