@@ -732,8 +732,9 @@ struct WsPlan {
   int64_t ipc;
   const void* fn;
   // Companion launch on the SMs the main launch leaves idle (clusters of 8 at one CTA per SM do not
-  // tile every GPC): clusters of kCompanionCy CTAs over the last `b2` volumes, or, for a single
-  // volume, its last `z2` output planes, run concurrently on a second stream. Both 0: none.
+  // tile every GPC): clusters of kCompanionCy CTAs over the last `b2` volumes, or, when the volumes
+  // are too few for that, the last `z2` output planes of every volume, run concurrently on a second
+  // stream. Both 0: none.
   int64_t b2;
   int64_t z2;
   int tiles_y2;
@@ -778,8 +779,8 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   const int64_t dz = z_end - z_begin;
   const int64_t min_ipc = 32;
   // Companion: when the main launch fills every cluster slot but leaves SMs idle, give the last b2
-  // volumes (a single volume: its last z2 planes) to clusters of 2 CTAs on those SMs. Their span is
-  // 32 rows, so a plane costs ty2 tiles instead of ty; the split balances the two launches'
+  // volumes (too few volumes: the last z2 planes of each) to clusters of 2 CTAs on those SMs. Their
+  // span is 32 rows, so a plane costs ty2 tiles instead of ty; the split balances the two launches'
   // cluster-steps (resident clusters / row tiles per plane each).
   int64_t b2 = 0, z2 = 0, nc2 = 0;
   int ty2 = 0;
@@ -793,12 +794,12 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
       if (nc2 >= 2) {
         ty2 = ws::tile_count(int(H), ws::TY * WsPlan::kCompanionCy, R, 1);
         const double r1 = double(maxc) / ty, r2 = double(nc2) / ty2;
-        if (B >= 2) {
-          b2 = int64_t(double(B) * r2 / (r1 + r2) + 0.5);
-          if (b2 > B - 1) b2 = B - 1;
-        } else {
-          // planes of one volume: each launch's segments start with a 2r-plane warm-up, so neither
-          // share may be tiny
+        b2 = int64_t(double(B) * r2 / (r1 + r2) + 0.5);
+        if (b2 > B - 1) b2 = B - 1;
+        if (b2 < 1) {
+          // too few volumes for a share of whole ones: the last planes of every volume instead; each
+          // launch's segments start with a 2r-plane warm-up, so neither share may be tiny
+          b2 = 0;
           z2 = int64_t(double(dz) * r2 / (r1 + r2) + 0.5);
           if (z2 < 8 || dz - z2 < 8) z2 = 0;
         }
@@ -806,7 +807,7 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
     }
     cudaGetLastError();
   }
-  const int64_t total = (B - b2) * int64_t(tx) * ty * (dz - z2);
+  const int64_t total = (B - b2) * int64_t(tx) * ty * (dz - z2);  // b2 and z2 are never both set
   int64_t nc = (total + min_ipc - 1) / min_ipc;
   if (nc > maxc) nc = maxc;
   if (nc < 1) nc = 1;
@@ -816,7 +817,7 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
     wp.b2 = b2;
     wp.z2 = z2;
     wp.tiles_y2 = ty2;
-    wp.total2 = (b2 > 0 ? b2 * dz : z2) * int64_t(tx) * ty2;
+    wp.total2 = (b2 > 0 ? b2 * dz : B * z2) * int64_t(tx) * ty2;
     wp.ipc2 = (wp.total2 + nc2 - 1) / nc2;
     wp.nclusters2 = (wp.total2 + wp.ipc2 - 1) / wp.ipc2;
   }
@@ -910,7 +911,7 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
   *nparts = wp.parts();
   const size_t esz = dtype == LNCC_F32 ? 4 : 2;
   ws::Args a1 = wa, a2 = wa;
-  if (wp.z2 > 0) {  // one volume: the main launch takes planes [z_begin, zs), the companion [zs, z_end)
+  if (wp.z2 > 0) {  // every volume: the main launch takes planes [z_begin, zs), the companion [zs, z_end)
     const int zs = wa.z_end - int(wp.z2);
     a1.z_end = zs;
     a2.z_begin = zs;
@@ -1110,6 +1111,7 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     wa.tiles_x = wp.tiles_x;
     wa.tiles_y = wp.tiles_y;
     wa.span_y = ws::TY * wp.cy;
+    wa.g_planes = int(z_end - z_begin);
     wa.total_items = wp.total;
     wa.items_per_cluster = wp.ipc;
     e = launch_ws(wp, wa, stream, B, D, H, W, dtype, &nparts);

@@ -65,6 +65,7 @@ struct Args {
   int z_begin, z_end;
   int tiles_x, tiles_y;
   int span_y;                 // 16 * cluster size
+  int g_planes;               // planes per volume of the gradient array (a launch may fill part of it)
   int64_t total_items;        // B * tiles_y * tiles_x * (z_end - z_begin)
   int64_t items_per_cluster;
 };
@@ -856,7 +857,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           if (X0 + CW * j >= sg.ox0 && X0 + CW * j < sg.ox1) om |= 1u << j;
       }
       const int64_t roff = om ? int64_t(Y) * W + X0 : 0;
-      S* __restrict__ G = reinterpret_cast<S*>(a.g) + sg.b * int64_t(Dout) * HW;
+      S* __restrict__ G = reinterpret_cast<S*>(a.g) + sg.b * int64_t(a.g_planes) * HW;
       const uint32_t tm = sm.tmem_base + (uint32_t(32 * (warp & 3)) << 16);
       const float gs = 2.f * a.gscale * (a.gscale_dev ? __ldg(a.gscale_dev) : 1.f);
       const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);

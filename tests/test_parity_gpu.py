@@ -356,14 +356,16 @@ def test_ws_repeat_bitwise():
         _lib.select_kernel(_lib.KERNEL_AUTO)
 
 
-# Companion launch: in a call with enough volumes the last ones (one volume: its last planes) run in
+# Companion launch: in a call with enough volumes the last ones (too few: the last planes of each) run in
 # clusters of 2 CTAs on the SMs that the main clusters leave idle, concurrently on a second stream. The
 # result must not depend on it.
 @pytest.mark.parametrize("shape,k,dtype", [((1, 8, 64, 128, 128), 7, torch.float32),
                                            ((3, 3, 64, 128, 128), 5, torch.float32),
                                            ((2, 8, 48, 128, 136), 9, torch.bfloat16),
-                                           # one volume: the companion takes the last planes
+                                           # too few volumes for a share of whole ones (one
+                                           # volume, or four): the companion takes the last planes
                                            ((1, 1, 512, 128, 128), 5, torch.float32),
+                                           ((1, 4, 128, 128, 128), 7, torch.float32),
                                            ((1, 1, 160, 256, 256), 7, torch.float32)])
 def test_ws_companion_matches_single_launch(shape, k, dtype):
     from fused_lncc import _lib, synth
