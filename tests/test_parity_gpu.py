@@ -366,6 +366,8 @@ def test_ws_repeat_bitwise():
                                            # volume, or four): the companion takes the last planes
                                            ((1, 1, 512, 128, 128), 5, torch.float32),
                                            ((1, 4, 128, 128, 128), 7, torch.float32),
+                                           # 256 rows: one cluster of 16 CTAs, bf16
+                                           ((1, 2, 128, 256, 128), 7, torch.bfloat16),
                                            ((1, 1, 160, 256, 256), 7, torch.float32)])
 def test_ws_companion_matches_single_launch(shape, k, dtype):
     from fused_lncc import _lib, synth
