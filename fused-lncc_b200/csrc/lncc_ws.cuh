@@ -617,6 +617,18 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           tm_st16(tmA + uint32_t(16 * f), v);
         }
       };
+      // the warm-up below loads its raw planes one after another: ask for all of them in L2 first
+      if (cm) {
+        for (int z = c0 - R; z <= c0 + R; ++z) {
+          if (z < 0 || z >= D) continue;
+#pragma unroll
+          for (int j = 0; j < NCH; ++j) {
+            if (!((cm >> j) & 1u)) continue;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(P + z * HW + roff + CW * j));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(T + z * HW + roff + CW * j));
+          }
+        }
+      }
       // zero the sums, then warm up over raw planes [c0 - R, c0 + R)
       tm_wait_st();
       {
