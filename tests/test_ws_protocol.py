@@ -183,6 +183,14 @@ def test_protocol_has_no_misaligned_arrivals_or_deadlock():
             assert waiting == 0, (R, seed)
 
 
+def test_protocol_with_16_ctas():
+    # planes of 129 - 256 rows run as one chain of up to 16 CTAs (non-portable cluster)
+    for seed in range(6):
+        violations, waiting = simulate(16, _steps(3), True, seed, slow_cta=seed % 16, seg_len=12 + 2 * 3)
+        assert not violations, (seed, violations[:3])
+        assert waiting == 0, seed
+
+
 def test_model_detects_halo_sent_only_for_valid_planes():
     # the rule the kernel does not use: the model must catch its misaligned arrivals
     hits = 0
