@@ -471,6 +471,8 @@ static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
 // ------------------------------------------------------------------------------------------------
 static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band, 3 warp-specialised
 static std::atomic<int> g_companion{1};      // warp-specialised kernel: companion launch on idle SMs
+// set by lncc_fused_forward_noalloc for its call: one launch, so no library stream or events to make
+static thread_local bool t_single_launch = false;
 
 // Row segments per column in the band kernel's column phases (threads = 128 * segments).
 // LNCC_BAND_SEGMENTS=2|4 overrides the default (a tuning knob; both variants compute the same).
@@ -784,7 +786,7 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   // cluster-steps (resident clusters / row tiles per plane each).
   int64_t b2 = 0, z2 = 0, nc2 = 0;
   int ty2 = 0;
-  if (cy >= 4 && B * int64_t(tx) * ty * dz >= min_ipc * maxc && g_companion.load()) {
+  if (cy >= 4 && B * int64_t(tx) * ty * dz >= min_ipc * maxc && g_companion.load() && !t_single_launch) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
@@ -1152,6 +1154,10 @@ int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype, 
                                int64_t H, int64_t W, int kernel_size, float smooth_dr, int64_t z_begin,
                                int64_t z_end, void* grad, float grad_scale, const float* grad_scale_dev,
                                double* cc_sum_out, float* loss_out, double loss_count, cudaStream_t stream) {
+  struct SingleLaunch {  // no companion launch: it would make a stream and events on first use
+    SingleLaunch() { t_single_launch = true; }
+    ~SingleLaunch() { t_single_launch = false; }
+  } single;
   const size_t cap = size_t(kNoAllocMaxPartials) * sizeof(double);
   const size_t need = lncc_workspace_bytes(B, D, H, W, kernel_size, dtype, z_begin, z_end);
   if (need > cap) return LNCC_ERR_TOO_LARGE;

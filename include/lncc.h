@@ -103,6 +103,8 @@ int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev,
  * first call on each device only looks up the array's device address (cudaGetSymbolAddress) with
  * that device current, so make that first call before capturing a stream into a CUDA graph. All
  * calls share the one array: calls that overlap on the GPU (different streams, no ordering) race.
+ * It always runs as a single launch on `stream` (never the companion launch of lncc_set_companion,
+ * which makes a stream and events of its own on first use).
  * Every other argument means exactly what it means for lncc_fused_forward.
  */
 int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype,

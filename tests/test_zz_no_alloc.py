@@ -34,7 +34,9 @@ def _call(lib, fn_name, p, t, k, with_workspace):
     return loss.item(), csum.item(), g
 
 
-@pytest.mark.parametrize("shape,k", [((2, 3, 24, 20, 28), 7), ((1, 2, 40, 64, 128), 5)])
+# the last shape is large enough for the regular entry point to add its companion launch; this one
+# stays a single launch on the caller's stream
+@pytest.mark.parametrize("shape,k", [((2, 3, 24, 20, 28), 7), ((1, 2, 40, 64, 128), 5), ((1, 8, 64, 128, 128), 7)])
 def test_noalloc_matches_workspace_entry_point_twice(shape, k):
     from fused_lncc import _lib
     lib = _lib.load()
@@ -45,7 +47,9 @@ def test_noalloc_matches_workspace_entry_point_twice(shape, k):
         l0, s0, g0 = _call(lib, "lncc_fused_forward", p, t, k, True)
         l1, s1, g1 = _call(lib, "lncc_fused_forward_noalloc", p, t, k, False)
         assert abs(l1 - l0) < FP32_LOSS_TOL, (call, l0, l1)
-        assert abs(s1 - s0) <= 1e-9 * max(1.0, abs(s0)), (call, s0, s1)
+        # a call this size may run in two launches through the regular entry point, whose different
+        # row tilings round the sum differently: the suite's 1e-6 relative bound for cc sums
+        assert abs(s1 - s0) <= 1e-6 * max(1.0, abs(s0)), (call, s0, s1)
         rel = ((g1.double() - g0.double()).norm() / g0.double().norm()).item()
         assert rel < FP32_REL, (call, rel)
 
