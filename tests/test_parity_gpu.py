@@ -395,6 +395,28 @@ def test_ws_companion_matches_single_launch(shape, k, dtype):
     assert cos > 0.99999 and rel < (1e-5 if dtype == torch.float32 else 5e-3), (cos, rel)
 
 
+@pytest.mark.parametrize("shape,k", [((1, 8, 64, 128, 128), 7), ((1, 1, 512, 128, 128), 5)])
+def test_ws_companion_loss_only(shape, k):
+    """Loss without gradient (the D group then only boxes its W-box share): the same sum with and
+    without the companion launch, and the companion runs for these shapes (volume split, plane split)."""
+    from fused_lncc import _lib, synth
+    pred, target = synth.blurred_pair(shape, device="cuda")
+    lib = _lib.load()
+    B, (D, H, W) = shape[0] * shape[1], shape[2:]
+    sums = []
+    for on in (True, False):
+        prev = _lib.set_companion(on)
+        try:
+            assert lib.lncc_launch_count(B, D, H, W, k, 0, 0, D, 0) == (2 if on else 1)
+            s = torch.zeros((), dtype=torch.float64, device="cuda")
+            lncc_fused(pred, target, k, grad=False, cc_sum_out=s)
+            torch.cuda.synchronize()
+            sums.append(s.item())
+        finally:
+            _lib.set_companion(prev)
+    assert abs(sums[0] - sums[1]) < 1e-6 * max(1.0, abs(sums[1])), sums
+
+
 def test_ws_companion_under_graph_capture():
     """The fork to the companion's stream and the join are captured like any stream work: a replay
     gives the eager result bit for bit (the stream and events were made by the eager call)."""
