@@ -474,7 +474,7 @@ def main():
         # which kernel the library picks for this shape (automatic choice, include/lncc.h): the
         # warp-specialised cluster kernel whenever W % 4 == 0 (torch allocations are aligned)
         kname = "lncc_ws_kernel" if W % 4 == 0 else "lncc_sweep_kernel"
-        launches_per_call = lib.lncc_launch_count(nb, D, H, W, k, dtc, z_rng[0], z_rng[1], 1)
+        launches_per_call = max(1, lib.lncc_launch_count(nb, D, H, W, k, dtc, z_rng[0], z_rng[1], 1))
         traffic = profile_traffic(kname, args.workload) if world == 1 else None
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,

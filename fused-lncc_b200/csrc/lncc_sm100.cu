@@ -1180,9 +1180,10 @@ int lncc_set_companion(int enable) { return g_companion.exchange(enable ? 1 : 0)
 
 int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, int dtype, int64_t z_begin,
                       int64_t z_end, int grad) {
-  if (!valid_k(kernel_size)) return LNCC_ERR_KERNEL_SIZE;
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
-  if (B < 1 || D < 1 || H < 1 || W < 1 || z_begin < 0 || z_end > D || z_end <= z_begin) return LNCC_ERR_BAD_ARG;
+  // errors are negative so that they never read as a count
+  if (!valid_k(kernel_size)) return -LNCC_ERR_KERNEL_SIZE;
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return -LNCC_ERR_DTYPE;
+  if (B < 1 || D < 1 || H < 1 || W < 1 || z_begin < 0 || z_end > D || z_end <= z_begin) return -LNCC_ERR_BAD_ARG;
   const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != 0, z_begin, z_end, nullptr, nullptr, nullptr);
   return (wp.ok && (wp.b2 > 0 || wp.z2 > 0)) ? 2 : 1;
 }

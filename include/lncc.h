@@ -169,7 +169,8 @@ int lncc_set_companion(int enable);
 
 /*
  * Kernel launches lncc_fused_forward makes for this shape with 16-byte-aligned tensors, not counting
- * the loss reduction: 2 when the companion launch runs, else 1; or a negative status. Diagnostics.
+ * the loss reduction: 2 when the companion launch runs, else 1; or minus an LNCC_ERR_* status for bad
+ * arguments. Diagnostics.
  */
 int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, int dtype,
                       int64_t z_begin, int64_t z_end, int grad);

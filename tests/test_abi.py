@@ -92,3 +92,18 @@ def test_scale_grad_rejects_bad_arguments(lib):
     assert lib.lncc_scale_grad(None, 0, 10, 8, None) == 1
     assert lib.lncc_scale_grad(8, 7, 10, 8, None) == 3
     assert lib.lncc_scale_grad(8, 0, 0, 8, None) == 0
+
+
+def test_companion_switch_and_launch_count_validation(lib):
+    # the switch is host state: it returns the previous setting
+    prev = lib.lncc_set_companion(0)
+    try:
+        assert lib.lncc_set_companion(1) == 0
+        assert lib.lncc_set_companion(0) == 1
+    finally:
+        lib.lncc_set_companion(prev)
+    # lncc_launch_count validates its arguments before asking the device anything; errors come back
+    # negated so that they cannot be mistaken for a launch count
+    assert lib.lncc_launch_count(1, 8, 8, 8, 4, 0, 0, 8, 1) == -2   # LNCC_ERR_KERNEL_SIZE
+    assert lib.lncc_launch_count(1, 8, 8, 8, 7, 5, 0, 8, 1) == -3   # LNCC_ERR_DTYPE
+    assert lib.lncc_launch_count(1, 8, 8, 8, 7, 0, 4, 4, 1) == -1   # LNCC_ERR_BAD_ARG (empty plane range)
