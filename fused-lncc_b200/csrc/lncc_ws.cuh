@@ -416,7 +416,9 @@ struct Seg {
   int xb, ox0, ox1;  // span column origin, output columns
 };
 
-template <int R, typename S, bool GRAD, int CW>
+// ASSIST: the D group boxes two of the five DW fields for the A group (always with the D running sums
+// in TMEM, k <= 7; a choice of the launch for k = 9, where they live in registers).
+template <int R, typename S, bool GRAD, int CW, bool ASSIST = true>
 __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   constexpr int NCH = VW / CW;  // global-memory chunks per lane
   constexpr int K = Geo<R>::K;
@@ -469,10 +471,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   cluster.sync();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-  // With the running D sums of the D group in TMEM (k <= 7), the D group also boxes fields 3 and 4
-  // (Stt, 2*Spt) of the A group's sums along W: A's W box is on the loop that bounds a step (A writes
-  // plane s+2 once the column groups release plane s), the D group idles while the column groups sweep.
-  constexpr bool DASSIST = Geo<R>::DSUM_TMEM;
+  // The D group also boxes fields 3 and 4 (Stt, 2*Spt) of the A group's sums along W: A's W box is on
+  // the loop that bounds a step (A writes plane s+2 once the column groups release plane s), the D group
+  // idles while the column groups sweep.
+  constexpr bool DASSIST = Geo<R>::DSUM_TMEM || ASSIST;
   constexpr int NFA = DASSIST ? 3 : 5;  // fields the A group boxes
   const float nf = a.n, nh = 0.5f * a.n, ndr = a.n * a.dr;
   double acc = 0.0;  // BC: loss partial
@@ -996,7 +998,13 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         for (int f = 0; f < 3; ++f)
 #pragma unroll
           for (int m = 0; m < 16; ++m) sum[f][m] = 0.f;
+        if constexpr (DASSIST) {  // the W-box share of the segment's first two steps
+          if (!d_part(s, plane_ok(0)) || !d_part(s + 1, plane_ok(1))) break;
+        }
         for (int it = 0; it < nsteps; ++it, ++s) {
+          if constexpr (DASSIST) {  // and of step s + 2 before step s's adjoints
+            if (it + 2 < nsteps && !d_part(s + 2, plane_ok(it + 2))) break;
+          }
           const int c = c0 + it;
           const bool cvalid = c >= 0 && c < D;
           const int o = c - R;
