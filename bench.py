@@ -4,11 +4,11 @@
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
 Prints ONE JSON line on rank 0. A step is one forward + backward of the loss through the public API.
-Volume workloads scale weakly: every rank owns a full batch of the workload's N*C volumes (its own
-seed), the loss is the mean over all ranks' volumes (one fp64 all-reduce), and `value` counts the
-voxels of all ranks. At N > 1 the line also carries `strong_scaling`: the same step over the one
-batch split across the ranks (the workload's volume sharding), timed the same way. D-slab workloads
-scale strongly: one volume split into D-slabs across the ranks.
+Every workload scales strongly: the workload's one batch is split across the ranks. Volume workloads
+shard the N*C volumes (rank r owns its share, the loss is the mean over the whole batch through one
+fp64 all-reduce); D-slab workloads split one volume into D-slabs. `value` counts the batch's voxels
+over the max-over-ranks step time. At N > 1 volume workloads also carry `weak_scaling`: every rank
+with a full batch of its own (its own seed), timed the same way.
 Timing: W untimed warm-up steps,
 then K steps each bracketed by CUDA events on the launching stream, an L2 flush (256 MiB write)
 before every step outside the events, barrier + synchronize around the whole timed region, max over
@@ -196,12 +196,15 @@ def _cpu_model():
     return None
 
 
+REFERENCE_MAX_STEPS = 40  # bounds the CPU arm at ~1 s per step
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     from fused_lncc import synth  # noqa: F401  (inputs only)
     pred, target, k, dtype = make_inputs(args.workload, "cpu")
-    steps = max(1, args.steps if args.steps <= 5 else 3)
+    steps = max(1, min(args.steps, REFERENCE_MAX_STEPS))
     value, info = cpu_reference_sample(pred, target, k, steps, max(1, min(args.warmup, 1)),
                                        sample_volumes=args.cpu_sample_volumes)
     shape = WORKLOADS[args.workload][0]
@@ -213,8 +216,12 @@ def run_reference(args, rank, world):
         "config": {"workload": args.workload, "shape": list(shape), "kernel_size": k,
                    "input_dtype": dtype, "sample_volumes": args.cpu_sample_volumes},
         "cpu_baseline": {"value": value, "unit": "Gvoxel/s", "cores": info["cores"], "kind": info["kind"],
-                         "sample": info["sample"], "cpu_model": info["cpu_model"]},
+                         "sample": info["sample"], "sample_volumes": args.cpu_sample_volumes,
+                         "cpu_model": info["cpu_model"]},
         "e2e": {"value": value, "unit": "Gvoxel/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        # each step is a per-voxel rate measured on sample_volumes of the workload's volumes; at most
+        # REFERENCE_MAX_STEPS steps are timed
+        "steps_requested": args.steps,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -258,16 +265,15 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     slabs = args.workload in SLAB_WORKLOADS
-    # slab workloads split one volume, so every rank builds the same one; volume workloads give each
-    # rank a batch of its own (seed 0 on rank 0: the one-GPU inputs)
-    pred, target, k, dtype = make_inputs(args.workload, dev, seed=0 if slabs else 1000 * rank)
+    # every rank builds the workload's one batch (seed 0) and keeps its share of it
+    pred, target, k, dtype = make_inputs(args.workload, dev, seed=0)
     shape = WORKLOADS[args.workload][0]
     n, c = shape[:2]
     nvol = n * c
     input_sha = None
-    if rank == 0 and args.workload == "config1":
-        input_sha = fused_lncc.synth.sha256_of(pred)
-    m_global = float(nvol if slabs else world * nvol) * shape[2] * shape[3] * shape[4]
+    if rank == 0 and args.workload in ("config1", "headline"):
+        input_sha = {"pred": fused_lncc.synth.sha256_of(pred), "target": fused_lncc.synth.sha256_of(target)}
+    m_global = float(nvol) * shape[2] * shape[3] * shape[4]
     if slabs:
         # one volume split into D-slabs; each rank keeps its owned planes plus 2r halo planes
         from fused_lncc.dist import SlabPlan, slab_lncc_loss
@@ -286,13 +292,13 @@ def main():
         def loss_fn(p, t):
             return slab_lncc_loss(p, t, plan, k)
     else:
-        b0, b1 = 0, nvol  # this rank's own batch
+        b0, b1 = volume_range(nvol, world, rank)  # this rank's share of the batch's volumes
         vshape = (nvol, 1, *shape[2:])
-        p_loc = pred.reshape(vshape).contiguous().requires_grad_(True)
-        t_loc = target.reshape(vshape).contiguous()
+        p_loc = pred.reshape(vshape)[b0:b1].contiguous().requires_grad_(True)
+        t_loc = target.reshape(vshape)[b0:b1].contiguous()
         z_rng = (0, shape[2])
         vox_local = p_loc.numel()
-        parallelism = f"data-parallel/{world} ({nvol} volumes per rank)"
+        parallelism = f"volume-sharded/{world} ({b1 - b0} of {nvol} volumes per rank)"
         if world > 1:
             def loss_fn(p, t):
                 return sharded_lncc_loss(p, t, k, m_global=m_global)
@@ -364,19 +370,20 @@ def main():
             ms_step = sum(s.elapsed_time(e) for s, e in evs) / len(evs)
             result["ms_step"] = max_over_ranks(ms_step)
             if world > 1 and not slabs:
-                # the BASELINE sharding as well: the one headline batch split across the ranks
-                # (strong scaling), this rank's share of its volumes, loss over the batch
-                sb0, sb1 = volume_range(nvol, world, rank)
-                p_s = p_loc.detach()[sb0:sb1].clone().requires_grad_(True)
-                t_s = t_loc[sb0:sb1].contiguous()
-                m_strong = float(nvol) * shape[2] * shape[3] * shape[4]
+                # weak scaling as well: every rank with a full batch of its own (its own seed), the
+                # loss over all ranks' volumes
+                pw, tw, _, _ = make_inputs(args.workload, dev, seed=1000 * (rank + 1))
+                p_s = pw.reshape(vshape).contiguous().requires_grad_(True)
+                t_s = tw.reshape(vshape).contiguous()
+                del pw, tw
+                m_weak = float(world * nvol) * shape[2] * shape[3] * shape[4]
 
-                def step_strong():
+                def step_weak():
                     p_s.grad = None
-                    sharded_lncc_loss(p_s, t_s, k, m_global=m_strong).backward()
+                    sharded_lncc_loss(p_s, t_s, k, m_global=m_weak).backward()
 
                 for _ in range(args.warmup):
-                    step_strong()
+                    step_weak()
                 torch.cuda.synchronize(dev)
                 barrier()
                 torch.cuda.synchronize(dev)
@@ -385,16 +392,16 @@ def main():
                     flush.zero_()
                     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     s.record(stream)
-                    step_strong()
+                    step_weak()
                     e.record(stream)
                     sev.append((s, e))
                 torch.cuda.synchronize(dev)
                 barrier()
                 torch.cuda.synchronize(dev)
                 ms_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in sev) / len(sev))
-                result["strong"] = {"value": m_strong / (ms_s * 1e-3) / 1e9, "unit": "Gvoxel/s",
-                                    "ms_per_step": ms_s, "volumes_per_rank": sb1 - sb0,
-                                    "global_batch": nvol}
+                result["weak"] = {"value": m_weak / (ms_s * 1e-3) / 1e9, "unit": "Gvoxel/s",
+                                  "ms_per_step": ms_s, "volumes_per_rank": nvol,
+                                  "global_batch": world * nvol}
                 del p_s, t_s
         # ---- roofline: the dominant kernel alone -----------------------------------------------------
         for _ in range(args.warmup):
@@ -463,7 +470,8 @@ def main():
         v, info = cpu_reference_sample(p_loc.detach(), t_loc, k, steps=3, warmup=1,
                                        sample_volumes=args.cpu_sample_volumes)
         cpu = {"value": v, "unit": "Gvoxel/s", "cores": info["cores"], "kind": info["kind"],
-               "sample": info["sample"], "cpu_model": info["cpu_model"]}
+               "sample": info["sample"], "sample_volumes": args.cpu_sample_volumes,
+               "cpu_model": info["cpu_model"]}
 
     if rank == 0:
         vox_global = m_global
@@ -480,11 +488,11 @@ def main():
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": result["ms_step"], "higher_is_better": True,
-            "scaling": "strong" if slabs else "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": args.workload, "shape": list(shape), "kernel_size": k,
                        "input_dtype": dtype, "volumes_per_rank": b1 - b0,
-                       "global_batch": nvol if slabs else world * nvol,
+                       "global_batch": nvol,
                        "parallelism": parallelism, "l2": "flushed (256 MiB write) before every step",
                        "input_sha256": input_sha},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -504,8 +512,8 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        if "strong" in result:
-            line["strong_scaling"] = result["strong"]
+        if "weak" in result:
+            line["weak_scaling"] = result["weak"]
         sys.stdout.flush()
         os.write(out_fd, (json.dumps(line) + "\n").encode())
     if world > 1:

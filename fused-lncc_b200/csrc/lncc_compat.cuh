@@ -9,7 +9,9 @@
 //
 // These are for debugging and for code written against the reference's extension (its tests call
 // lncc_forward / box3d_sep_forward directly). The training path is the fused kernel, which
-// materialises nothing.
+// materialises nothing. The maps forward also serves the per-voxel loss (reduction 'none'): it can
+// write 1 - ncc instead of ncc, and weight the adjoints by an upstream gradient map G at each voxel,
+// so that the maps backward with scale -1 gives d(sum_v G(v) * (1 - ncc(v)))/dpred.
 //
 // One kernel template, three epilogues. A block owns a TH x TW tile of output columns (H, W) of one
 // volume and a chunk of up to ZCHUNK output planes. Each thread owns a few columns of the
@@ -36,6 +38,8 @@ struct Args {
   const void* p;       // BWD: pred and target at the output voxel (S)
   const void* t;
   void* out[4];        // MAPS: ncc, A, Bc, Cc (fp32, each may be null); BWD: grad (S); BOX: y (fp32)
+  const float* wmap;   // MAPS: null, or a (B, D, H, W) fp32 map multiplying A, Bc, Cc voxel by voxel
+  int loss_map;        // MAPS: out[0] receives 1 - ncc instead of ncc
   int D, H, W;
   int tiles_x, tiles_y, chunks;
   float n, ndr, scale;
@@ -164,7 +168,13 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
         } else if (cc >= 1.f) {
           cc = 1.f;
         }
-        if (a.out[0]) static_cast<float*>(a.out[0])[o] = cc;
+        if (a.wmap) {
+          const float gw = __ldg(a.wmap + o);
+          A *= gw;
+          Bc *= gw;
+          Cc *= gw;
+        }
+        if (a.out[0]) static_cast<float*>(a.out[0])[o] = a.loss_map ? 1.f - cc : cc;
         if (a.out[1]) static_cast<float*>(a.out[1])[o] = A;
         if (a.out[2]) static_cast<float*>(a.out[2])[o] = Bc;
         if (a.out[3]) static_cast<float*>(a.out[3])[o] = Cc;

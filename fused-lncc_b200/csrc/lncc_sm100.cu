@@ -34,7 +34,6 @@
 
 #define LNCC_VERSION_NUM 100  // 0.1.0
 
-#include "lncc_band.cuh"
 #include "lncc_compat.cuh"
 #include "lncc_ws.cuh"
 
@@ -90,6 +89,7 @@ struct SweepArgs {
   int D, H, W;
   int z_begin, z_end, dchunk;
   int tiles_w, tiles_h, nchunks;
+  unsigned* abort_word;  // workspace word that lncc_check_abort reads; this kernel never waits, so it only clears it
 };
 
 template <int R, int TH, int TW, int NT, typename S, bool GRAD>
@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
   const int zs = a.z_begin + ch * a.dchunk;
   const int ze = min(zs + a.dchunk, a.z_end);
   const int D = a.D, H = a.H, W = a.W;
+  if (a.abort_word && tid == 0 && blockIdx.x == 0) *a.abort_word = 0u;
   const int64_t HW = int64_t(H) * W;
   const S* __restrict__ P = reinterpret_cast<const S*>(a.p) + b * D * HW;
   const S* __restrict__ T = reinterpret_cast<const S*>(a.t) + b * D * HW;
@@ -466,164 +467,17 @@ static size_t smem_needed(int R) {
 
 static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
 
+// Workspace layout: a 16-byte header whose first word records a timed-out wait of the last call
+// (lncc_check_abort), then the fp64 loss partials.
+constexpr size_t kWsHeader = 16;
+
 // ------------------------------------------------------------------------------------------------
-// band kernel host side
+// process-wide switches
 // ------------------------------------------------------------------------------------------------
-static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 2 band, 3 warp-specialised
+static std::atomic<int> g_kernel_choice{0};  // 0 auto, 1 sweep, 3 warp-specialised (2: retired)
 static std::atomic<int> g_companion{1};      // warp-specialised kernel: companion launch on idle SMs
 // set by lncc_fused_forward_noalloc for its call: one launch, so no library stream or events to make
 static thread_local bool t_single_launch = false;
-
-// Row segments per column in the band kernel's column phases (threads = 128 * segments).
-// LNCC_BAND_SEGMENTS=2|4 overrides the default (a tuning knob; both variants compute the same).
-static int band_segments() {
-  static const int v = [] {
-    const char* e = getenv("LNCC_BAND_SEGMENTS");
-    const int x = e ? atoi(e) : 4;
-    return (x == 2 || x == 4) ? x : 4;
-  }();
-  return v;
-}
-
-template <int R, typename S, bool GRAD, int NSEG>
-static cudaError_t band_prepare(const void** fn_out) {
-  auto kfn = band::lncc_band_kernel<R, S, GRAD, NSEG>;
-  static std::atomic<uint64_t> done{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
-  if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, band::smem_bytes<R>());
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    done.fetch_or(bit, std::memory_order_acq_rel);
-  }
-  *fn_out = reinterpret_cast<const void*>(kfn);
-  return cudaSuccess;
-}
-
-template <typename S, bool GRAD, int NSEG>
-static cudaError_t band_fn_seg(int R, const void** fn) {
-  switch (R) {
-    case 1: return band_prepare<1, S, GRAD, NSEG>(fn);
-    case 2: return band_prepare<2, S, GRAD, NSEG>(fn);
-    case 3: return band_prepare<3, S, GRAD, NSEG>(fn);
-    case 4: return band_prepare<4, S, GRAD, NSEG>(fn);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
-template <typename S, bool GRAD>
-static cudaError_t band_fn(int R, const void** fn) {
-  return band_segments() == 2 ? band_fn_seg<S, GRAD, 2>(R, fn) : band_fn_seg<S, GRAD, 4>(R, fn);
-}
-
-static cudaError_t band_kernel_fn(int R, int dtype, bool grad, const void** fn) {
-  if (dtype == LNCC_F32) return grad ? band_fn<float, true>(R, fn) : band_fn<float, false>(R, fn);
-  return grad ? band_fn<__nv_bfloat16, true>(R, fn) : band_fn<__nv_bfloat16, false>(R, fn);
-}
-
-static bool band_supported(int64_t H, int64_t W, int dtype, const void* p, const void* t, const void* g) {
-  if (W > band::WMAX || (W % 4) != 0) return false;
-  if (H > int64_t(band::TH) * 16) return false;
-  const uintptr_t al = dtype == LNCC_F32 ? 16 : 8;
-  if ((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al))) return false;
-  return true;
-}
-
-// Number of clusters that fit on the device at once (cached per device / cluster size / variant).
-static int band_smem_for(int R) {
-  switch (R) {
-    case 1: return band::smem_bytes<1>();
-    case 2: return band::smem_bytes<2>();
-    case 3: return band::smem_bytes<3>();
-    default: return band::smem_bytes<4>();
-  }
-}
-
-static int band_max_clusters(const void* fn, int cy, int cy_r) {
-  static std::mutex mu;
-  struct Key { int dev; int cy; const void* fn; int val; };
-  static Key cache[64];
-  static int ncache = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  std::lock_guard<std::mutex> lk(mu);
-  for (int i = 0; i < ncache; ++i)
-    if (cache[i].dev == dev && cache[i].cy == cy && cache[i].fn == fn) return cache[i].val;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(cy);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(unsigned(cy), 1, 1);
-  cfg.blockDim = dim3(band::NT, 1, 1);
-  cfg.dynamicSmemBytes = size_t(band_smem_for(cy_r));
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n < 1) {
-    cudaGetLastError();
-    n = 0;
-  }
-  if (ncache < 64) cache[ncache++] = {dev, cy, fn, n};
-  return n;
-}
-
-struct BandPlan {
-  bool ok;
-  int R;
-  int cy;
-  int64_t nclusters;
-  int64_t ppc;
-  const void* fn;
-};
-
-static BandPlan make_band_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bool grad, int64_t z_begin,
-                               int64_t z_end, const void* p, const void* t, const void* g) {
-  BandPlan bp{false, k / 2, 0, 0, 0, nullptr};
-  const int choice = g_kernel_choice.load();
-  if (choice == 1 || choice == 3) return bp;
-  if (!band_supported(H, W, dtype, p, t, g)) return bp;
-  const void* fn = nullptr;
-  if (band_kernel_fn(k / 2, dtype, grad, &fn) != cudaSuccess) return bp;
-  const int cy = int((H + band::TH - 1) / band::TH);
-  const int maxc = band_max_clusters(fn, cy, k / 2);
-  if (maxc < 1) return bp;
-  const int64_t total = B * (z_end - z_begin);
-  const int64_t min_ppc = 32;
-  int64_t nc = (total + min_ppc - 1) / min_ppc;
-  if (nc > maxc) nc = maxc;
-  if (nc < 1) nc = 1;
-  const int64_t ppc = (total + nc - 1) / nc;
-  nc = (total + ppc - 1) / ppc;
-  bp.ok = true;
-  bp.cy = cy;
-  bp.nclusters = nc;
-  bp.ppc = ppc;
-  bp.fn = fn;
-  return bp;
-}
-
-static cudaError_t launch_band(const BandPlan& bp, const band::BandArgs& ba, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(bp.cy);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(unsigned(bp.cy), unsigned(bp.nclusters), 1);
-  cfg.blockDim = dim3(band::NT, 1, 1);
-  cfg.dynamicSmemBytes = size_t(band_smem_for(bp.R));
-  cfg.stream = st;
-  void* args[] = {const_cast<band::BandArgs*>(&ba)};
-  return cudaLaunchKernelExC(&cfg, bp.fn, args);
-}
 
 // ------------------------------------------------------------------------------------------------
 // warp-specialised cluster kernel host side (lncc_ws.cuh)
@@ -752,14 +606,18 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
                            int64_t z_end, const void* p, const void* t, const void* g) {
   WsPlan wp{false, k / 2, 0, 0, 0, 0, 0, 0, nullptr, 0, 0, 0, 0, 0, 0};
   const int choice = g_kernel_choice.load();
-  if (choice == 1 || choice == 2) return wp;
+  if (choice == 1) return wp;
   // pointers unknown (workspace query): plan as for aligned tensors
   const int cw = (p == nullptr && t == nullptr) ? ((W % 8 == 0) ? 8 : (W % 4 == 0) ? 4 : 0)
                                                  : ws_chunk(W, dtype, p, t, g);
   if (cw == 0) return wp;
+  // k = 9 compiles the kernel twice: with the D group's W-box share (it pays in clusters of up to 8
+  // CTAs; measured: the MRI batch +3.7%) and without it (taller clusters: one 256^3 volume +4.7%).
+  // Every occupancy query below is made on the variant that the launch of that cluster size uses.
   const void* fn = nullptr;
-  // the variant without the D group's W-box share for the occupancy queries (the same resources)
-  if (ws_kernel_fn(k / 2, dtype, grad, cw, false, &fn) != cudaSuccess) {
+  const void* fn_tall = nullptr;
+  if (ws_kernel_fn(k / 2, dtype, grad, cw, true, &fn) != cudaSuccess ||
+      ws_kernel_fn(k / 2, dtype, grad, cw, false, &fn_tall) != cudaSuccess) {
     cudaGetLastError();
     return wp;
   }
@@ -775,11 +633,12 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   // cluster are fewer (every cluster advances one tile-plane per step whatever its height).
   if (H > int64_t(ws::TY) * kWsMaxCluster && H <= int64_t(ws::TY) * kWsMaxTall) {
     const int cyt = int((H + ws::TY - 1) / ws::TY);
-    const int maxt = ws_max_clusters(fn, cyt, R);
+    const int maxt = ws_max_clusters(fn_tall, cyt, R);
     if (maxt >= 1 && 1.0 / maxt < double(ty) / maxc) {
       cy = cyt;
       ty = 1;
       maxc = maxt;
+      fn = fn_tall;
     }
   }
   const int64_t dz = z_end - z_begin;
@@ -834,15 +693,6 @@ static WsPlan make_ws_plan(int64_t B, int64_t H, int64_t W, int k, int dtype, bo
   wp.total = total;
   wp.nclusters = nc;
   wp.ipc = ipc;
-  // k = 9: the D group's W-box share pays in clusters of up to 8 CTAs and costs in taller ones
-  // (measured: the MRI batch +3.7%, one 256^3 volume -4.7%)
-  if (R == 4 && cy <= kWsMaxCluster) {
-    const void* fa = nullptr;
-    if (ws_kernel_fn(R, dtype, grad, cw, true, &fa) == cudaSuccess)
-      fn = fa;
-    else
-      cudaGetLastError();
-  }
   wp.fn = fn;
   return wp;
 }
@@ -865,36 +715,34 @@ static cudaError_t launch_ws_grid(const WsPlan& wp, int cy, int64_t nclusters, c
   return cudaLaunchKernelExC(&cfg, wp.fn, args);
 }
 
-// Per-device stream for the companion launch, and per-thread fork / join events (no timing), made on
-// first use outside stream capture and kept for the life of the process. Returns false when they
-// cannot be had, in which case the caller runs the main launch over every volume.
+// Stream for the companion launch and fork / join events (no timing), per host thread and device,
+// made on first use outside stream capture and kept for the life of the thread (a stream captured into
+// one thread's graph is never touched by another thread's call). Returns false when they cannot be
+// had, in which case the caller runs the main launch over every volume.
 static bool companion_resources(int dev, bool create, cudaStream_t* comp, cudaEvent_t* fork,
                                 cudaEvent_t* join) {
-  static std::mutex mu;
-  static cudaStream_t streams[64] = {nullptr};
-  thread_local cudaEvent_t ev[64][2] = {};
+  struct Res {
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+  };
+  thread_local Res res[64];
   if (dev < 0 || dev >= 64) return false;
-  if (!ev[dev][0]) {
+  Res& r = res[dev];
+  if (!r.st) {
     if (!create) return false;
-    if (cudaEventCreateWithFlags(&ev[dev][0], cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ev[dev][1], cudaEventDisableTiming) != cudaSuccess) {
+    if (cudaEventCreateWithFlags(&r.ev[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&r.ev[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&r.st, cudaStreamNonBlocking) != cudaSuccess) {
       cudaGetLastError();
-      ev[dev][0] = ev[dev][1] = nullptr;
+      if (r.ev[0]) cudaEventDestroy(r.ev[0]);
+      if (r.ev[1]) cudaEventDestroy(r.ev[1]);
+      r = Res();
       return false;
     }
   }
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!streams[dev] && !create) return false;
-    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
-      cudaGetLastError();
-      streams[dev] = nullptr;
-      return false;
-    }
-    *comp = streams[dev];
-  }
-  *fork = ev[dev][0];
-  *join = ev[dev][1];
+  *comp = r.st;
+  *fork = r.ev[0];
+  *join = r.ev[1];
   return true;
 }
 
@@ -942,6 +790,7 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
   if (e == cudaSuccess) e = launch_ws_grid(wp, wp.cy, wp.nclusters, a1, st);
   if (e == cudaSuccess) {
     a2.partials = wa.partials + int64_t(wp.cy) * wp.nclusters;
+    a2.clear_abort = 0;  // the main launch clears the word; both may set it
     a2.tiles_y = wp.tiles_y2;
     a2.span_y = ws::TY * WsPlan::kCompanionCy;
     a2.total_items = wp.total2;
@@ -1028,6 +877,7 @@ const char* lncc_strerror(int status) {
     case LNCC_ERR_WORKSPACE: return "fused_lncc: workspace missing or too small";
     case LNCC_ERR_CUDA: return "fused_lncc: CUDA runtime error";
     case LNCC_ERR_TOO_LARGE: return "fused_lncc: size exceeds the fixed maximum of this entry point";
+    case LNCC_ERR_ABORTED: return "fused_lncc: a bounded wait in the kernel timed out; the results of that call are invalid";
     default: return "fused_lncc: unknown status";
   }
 }
@@ -1046,15 +896,7 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
     const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, gflag != 0, z_begin, z_end, nullptr, nullptr, nullptr);
     if (wp.ok && size_t(wp.parts()) * sizeof(double) > need) need = size_t(wp.parts()) * sizeof(double);
   }
-  const BandPlan bp = make_band_plan(B, H, W, kernel_size, dtype, true, z_begin, z_end, nullptr, nullptr, nullptr);
-  if (bp.ok) {
-    const size_t nb = size_t(bp.cy) * size_t(bp.nclusters) * sizeof(double);
-    if (nb > need) need = nb;
-    const BandPlan bq = make_band_plan(B, H, W, kernel_size, dtype, false, z_begin, z_end, nullptr, nullptr, nullptr);
-    if (bq.ok && size_t(bq.cy) * size_t(bq.nclusters) * sizeof(double) > need)
-      need = size_t(bq.cy) * size_t(bq.nclusters) * sizeof(double);
-  }
-  return need;
+  return need + kWsHeader;
 }
 
 int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
@@ -1074,10 +916,8 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
   if (pl.nblocks > INT32_MAX) return LNCC_ERR_TOO_LARGE;
   const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
-  BandPlan bp{false, kernel_size / 2, 0, 0, 0, nullptr};
-  if (!wp.ok) bp = make_band_plan(B, H, W, kernel_size, dtype, grad != nullptr, z_begin, z_end, pred, target, grad);
-  int64_t nparts = wp.ok ? wp.parts() : bp.ok ? int64_t(bp.cy) * bp.nclusters : pl.nblocks;
-  const size_t need = size_t(nparts) * sizeof(double);
+  int64_t nparts = wp.ok ? wp.parts() : pl.nblocks;
+  const size_t need = size_t(nparts) * sizeof(double) + kWsHeader;
   if (!workspace || workspace_bytes < need || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
   if (loss_out && !(loss_count > 0.0)) return LNCC_ERR_BAD_ARG;
 
@@ -1091,7 +931,8 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
   a.p = pred;
   a.t = target;
   a.g = grad;
-  a.partials = reinterpret_cast<double*>(workspace);
+  a.partials = reinterpret_cast<double*>(static_cast<char*>(workspace) + kWsHeader);
+  a.abort_word = static_cast<unsigned*>(workspace);
   a.gscale_dev = grad_scale_dev;
   a.gscale = grad_scale;
   a.n = float(kernel_size * kernel_size * kernel_size);
@@ -1114,6 +955,8 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     wa.t = target;
     wa.g = grad;
     wa.partials = a.partials;
+    wa.abort_word = a.abort_word;
+    wa.clear_abort = 1;
     wa.gscale_dev = grad_scale_dev;
     wa.gscale = grad_scale;
     wa.n = a.n;
@@ -1130,24 +973,6 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     wa.total_items = wp.total;
     wa.items_per_cluster = wp.ipc;
     e = launch_ws(wp, wa, stream, B, D, H, W, dtype, &nparts);
-  } else if (bp.ok) {
-    band::BandArgs ba;
-    ba.p = pred;
-    ba.t = target;
-    ba.g = grad;
-    ba.partials = a.partials;
-    ba.gscale_dev = grad_scale_dev;
-    ba.gscale = grad_scale;
-    ba.n = a.n;
-    ba.dr = smooth_dr;
-    ba.D = int(D);
-    ba.H = int(H);
-    ba.W = int(W);
-    ba.z_begin = int(z_begin);
-    ba.z_end = int(z_end);
-    ba.total_planes = B * (z_end - z_begin);
-    ba.planes_per_cluster = bp.ppc;
-    e = launch_band(bp, ba, stream);
   } else if (dtype == LNCC_F32)
     e = g ? dispatch_r<float, true>(pl.R, a, pl.nblocks, stream)
           : dispatch_r<float, false>(pl.R, a, pl.nblocks, stream);
@@ -1177,14 +1002,34 @@ int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype, 
   double* scratch = nullptr;
   const int st = noalloc_scratch(&scratch);
   if (st != LNCC_OK) return st;
-  // need == 0 means invalid arguments: the regular entry point reports the precise status
-  return lncc_fused_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, z_begin, z_end, grad,
-                            grad_scale, grad_scale_dev, cc_sum_out, loss_out, loss_count, scratch, cap,
-                            stream);
+  // need == 0 means invalid arguments: the regular entry point reports the precise status. The
+  // regular entry point re-plans with the real pointers; a plan needing more partials than the fixed
+  // array holds is a size beyond this entry point's maximum, not a caller's workspace error.
+  const int r = lncc_fused_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, z_begin, z_end,
+                                   grad, grad_scale, grad_scale_dev, cc_sum_out, loss_out, loss_count, scratch,
+                                   cap, stream);
+  return r == LNCC_ERR_WORKSPACE ? LNCC_ERR_TOO_LARGE : r;
+}
+
+int lncc_check_abort(const void* workspace, cudaStream_t stream) {
+  if (!workspace || (uintptr_t(workspace) % 8)) return LNCC_ERR_BAD_ARG;
+  unsigned w = 0;
+  if (cudaMemcpyAsync(&w, workspace, sizeof(w), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return LNCC_ERR_CUDA;
+  return w ? LNCC_ERR_ABORTED : LNCC_OK;
+}
+
+int lncc_wait_timeout_selftest(void* workspace, size_t workspace_bytes, unsigned limit_us, cudaStream_t stream) {
+  if (!workspace || workspace_bytes < kWsHeader || (uintptr_t(workspace) % 8)) return LNCC_ERR_WORKSPACE;
+  if (limit_us == 0 || limit_us > 10000000u) return LNCC_ERR_BAD_ARG;
+  ws::wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(static_cast<unsigned*>(workspace),
+                                                         (unsigned long long)limit_us * 1000ull);
+  return cudaGetLastError() == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 int lncc_select_kernel(int which) {
-  if (which < 0 || which > 3) return LNCC_ERR_BAD_ARG;
+  if (which < 0 || which > 3 || which == 2) return LNCC_ERR_BAD_ARG;
   g_kernel_choice.store(which);
   return LNCC_OK;
 }
@@ -1261,6 +1106,76 @@ int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_
   a.in[0] = x;
   a.out[0] = y;
   const cudaError_t e = launch_compat<compat::BOX, float>(kernel_size / 2, a, nb, stream);
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+size_t lncc_loss_map_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W) {
+  if (B < 1 || D < 1 || H < 1 || W < 1) return 0;
+  return size_t(3) * size_t(B) * size_t(D) * size_t(H) * size_t(W) * sizeof(float);
+}
+
+int lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                          int64_t W, int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream) {
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!pred || !target || !loss_map) return LNCC_ERR_BAD_ARG;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(loss_map) % 4)) return LNCC_ERR_BAD_ARG;
+  a.in[0] = pred;
+  a.in[1] = target;
+  a.out[0] = loss_map;
+  a.loss_map = 1;
+  a.ndr = a.n * smooth_dr;
+  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
+                                          : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
+                           int64_t D, int64_t H, int64_t W, int kernel_size, float smooth_dr, void* grad,
+                           float* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!grad_map || !pred || !target || !grad) return LNCC_ERR_BAD_ARG;
+  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(grad) % esz) ||
+      (uintptr_t(grad_map) % 4))
+    return LNCC_ERR_BAD_ARG;
+  const size_t need = lncc_loss_map_scratch_bytes(B, D, H, W);
+  if (!scratch || scratch_bytes < need || (uintptr_t(scratch) % 4)) return LNCC_ERR_WORKSPACE;
+  const size_t nvox = need / (3 * sizeof(float));
+  float* mA = scratch;
+  float* mB = scratch + nvox;
+  float* mC = scratch + 2 * nvox;
+  // G-weighted adjoint maps at every voxel, then -(box(G*A) + 2p*box(G*Bc) + t*box(G*Cc))
+  a.in[0] = pred;
+  a.in[1] = target;
+  a.out[1] = mA;
+  a.out[2] = mB;
+  a.out[3] = mC;
+  a.wmap = grad_map;
+  a.ndr = a.n * smooth_dr;
+  cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
+                                    : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
+  compat::Args b = a;
+  b.in[0] = mA;
+  b.in[1] = mB;
+  b.in[2] = mC;
+  b.p = pred;
+  b.t = target;
+  b.out[0] = grad;
+  b.out[1] = b.out[2] = b.out[3] = nullptr;
+  b.wmap = nullptr;
+  b.scale = -1.f;
+  e = dtype == LNCC_F32 ? launch_compat<compat::BWD, float>(kernel_size / 2, b, nb, stream)
+                        : launch_compat<compat::BWD, __nv_bfloat16>(kernel_size / 2, b, nb, stream);
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 

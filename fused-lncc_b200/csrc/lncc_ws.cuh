@@ -68,6 +68,8 @@ struct Args {
   int g_planes;               // planes per volume of the gradient array (a launch may fill part of it)
   int64_t total_items;        // B * tiles_y * tiles_x * (z_end - z_begin)
   int64_t items_per_cluster;
+  unsigned* abort_word;       // workspace word: set to 1 by a CTA whose bounded wait ran out
+  int clear_abort;            // this launch's first CTA zeroes abort_word at its start
 };
 
 template <int R>
@@ -253,12 +255,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 // Slow path of mbar_wait: poll for at most kWaitLimitNs; on timeout set the CTA's abort flag, after
 // which every wait of the CTA returns at once and the roles leave their loops (NaN loss partial).
-__device__ __forceinline__ void mbar_wait_slow(uint32_t a, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ void mbar_wait_slow(uint32_t a, uint32_t parity, volatile int* abort_flag,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long t0 = global_ns();
   for (;;) {
     if (mbar_test(a, parity)) return;
     if (*abort_flag) return;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       return;
     }
@@ -435,6 +438,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   const int D = a.D, H = a.H, W = a.W;
   const int64_t HW = int64_t(H) * W;
   const int Dout = a.z_end - a.z_begin;
+  // every wait below is bounded by seconds, so this clear precedes any CTA's abort record
+  if (a.clear_abort && a.abort_word && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) *a.abort_word = 0u;
   volatile int* abort_flag = &sm.abort_flag;
   const uint32_t bar0 = smem_addr(&sm.bar[0]);
   auto bar = [&](int which, int i) -> uint32_t { return bar0 + uint32_t(8 * (which + i)); };
@@ -1088,9 +1093,31 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
   if (tid == 0) {
     double tot = 0.0;
     for (int w = 0; w < 8; ++w) tot += sm.red[w];
-    if (sm.abort_flag) tot = __longlong_as_double(0x7ff8000000000000ll);  // NaN: a wait timed out
+    if (sm.abort_flag) {  // a wait timed out: NaN partial, and the abort word for callers without a loss
+      tot = __longlong_as_double(0x7ff8000000000000ll);
+      if (a.abort_word) atomicOr(a.abort_word, 1u);
+    }
     a.partials[int64_t(blockIdx.y) * gridDim.x + blockIdx.x] = tot;
   }
+}
+
+// Self-test of the bounded wait and of the abort record: one warp waits on a barrier that nothing
+// arrives at, with a limit of `limit_ns`; the wait gives up, and the warp records the abort in
+// `word` exactly as the fused kernel's teardown does. No cluster, bulk copy or TMEM is involved.
+__global__ void __launch_bounds__(32, 1) wait_timeout_selftest_kernel(unsigned* word, unsigned long long limit_ns) {
+  __shared__ unsigned long long bar;
+  __shared__ int abort_flag;
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    *word = 0u;
+    abort_flag = 0;
+    mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  mbar_wait_slow(b, 0u, &abort_flag, limit_ns);  // phase 0 never completes
+  __syncwarp();
+  if (threadIdx.x == 0 && abort_flag) atomicOr(word, 1u);
 }
 
 }  // namespace ws

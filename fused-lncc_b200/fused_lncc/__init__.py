@@ -6,6 +6,9 @@ Drop-in for the reference package (reference fused_lncc/__init__.py:77-83):
     loss = fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5)   # 1 - mean(cc)
     loss.backward()                                                        # grad for pred only
 
+`reduction` ('mean' default, 'sum', 'none') is an addition the reference lists as open
+(reference BENCHMARKS.md:177-178): 'sum' gives sum(1 - cc), 'none' the per-voxel map 1 - cc.
+
 Same signature, defaults, assertion errors, RuntimeErrors, fp32 scalar result and pred-dtype
 gradient as the reference. Inside, the forward is ONE kernel pass that also produces dL/dpred.
 The backward is then one tiny launch that returns immediately when grad_out == 1. The reference
@@ -16,7 +19,9 @@ import torch
 
 from . import _lib
 
-__all__ = ["fused_lncc_loss", "lncc_fused", "FusedLNCC", "compat"]
+__all__ = ["fused_lncc_loss", "lncc_fused", "loss_map", "FusedLNCC", "FusedLNCCMap", "compat"]
+
+REDUCTIONS = {"mean": 0, "sum": 1}  # the fused kernel's reductions; 'none' has its own path
 
 _DTYPES = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16}
 
@@ -111,18 +116,85 @@ def scale_grad_(grad, grad_out):
 # registers fused_lncc::forward/backward for the same reason, fused_lncc/__init__.py:22-46).
 @torch.library.custom_op("fused_lncc::fwd_grad", mutates_args=())
 def _fwd_grad_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float,
-                 need_grad: bool) -> tuple[torch.Tensor, torch.Tensor]:
-    loss, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=need_grad)
+                 need_grad: bool, reduction: int) -> tuple[torch.Tensor, torch.Tensor]:
+    if reduction == REDUCTIONS["sum"]:
+        # sum(1 - cc) = M - sum(cc): the gradient of -sum(cc), the loss from the fp64 cc sum
+        cs = torch.empty((), dtype=torch.float64, device=pred.device)
+        _, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=need_grad, grad_scale=-1.0,
+                          cc_sum_out=cs)
+        loss = (float(pred.numel()) - cs).to(torch.float32)
+    else:
+        loss, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=need_grad)
     if g is None:
         g = pred.new_empty((0,))
     return loss, g
 
 
 @_fwd_grad_op.register_fake
-def _(pred, target, kernel_size, smooth_dr, need_grad):
+def _(pred, target, kernel_size, smooth_dr, need_grad, reduction):
     loss = pred.new_empty((), dtype=torch.float32)  # the loss is fp32 even for bf16 input
     g = torch.empty_like(pred) if need_grad else pred.new_empty((0,))
     return loss, g
+
+
+def loss_map(pred, target, kernel_size=7, smooth_dr=1e-5):
+    """Per-voxel loss 1 - cc (cc clamped to 1, NaN kept), an fp32 tensor of pred's shape."""
+    _check_pair(pred, target)
+    *lead, D, H, W = pred.shape
+    B = 1
+    for s_ in lead:
+        B *= int(s_)
+    out = torch.empty(pred.shape, dtype=torch.float32, device=pred.device)
+    lib = _lib.load()
+    with torch.cuda.device(pred.device):
+        st = lib.lncc_loss_map_forward(pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype], B, D, H, W,
+                                       int(kernel_size), float(smooth_dr), out.data_ptr(),
+                                       torch.cuda.current_stream(pred.device).cuda_stream)
+    _lib.check(st, "fused_lncc loss_map")
+    return out
+
+
+def loss_map_backward(grad_map, pred, target, kernel_size=7, smooth_dr=1e-5):
+    """d(sum(grad_map * loss_map(pred, target)))/dpred, in pred's dtype."""
+    _check_pair(pred, target)
+    if grad_map.shape != pred.shape:
+        raise RuntimeError("fused_lncc: grad_map must have pred's shape")
+    gm = grad_map.to(device=pred.device, dtype=torch.float32).contiguous()
+    *lead, D, H, W = pred.shape
+    B = 1
+    for s_ in lead:
+        B *= int(s_)
+    lib = _lib.load()
+    g = torch.empty_like(pred)
+    with torch.cuda.device(pred.device):
+        nb = lib.lncc_loss_map_scratch_bytes(B, D, H, W)
+        scratch = torch.empty(max(nb, 4) // 4, dtype=torch.float32, device=pred.device)
+        st = lib.lncc_loss_map_backward(gm.data_ptr(), pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype],
+                                        B, D, H, W, int(kernel_size), float(smooth_dr), g.data_ptr(),
+                                        scratch.data_ptr(), nb, torch.cuda.current_stream(pred.device).cuda_stream)
+    _lib.check(st, "fused_lncc loss_map_backward")
+    return g
+
+
+@torch.library.custom_op("fused_lncc::loss_map", mutates_args=())
+def _loss_map_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float) -> torch.Tensor:
+    return loss_map(pred, target, kernel_size, smooth_dr)
+
+
+@_loss_map_op.register_fake
+def _(pred, target, kernel_size, smooth_dr):
+    return pred.new_empty(pred.shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("fused_lncc::loss_map_backward", mutates_args=())
+def _loss_map_bwd_op(grad_map: torch.Tensor, pred: torch.Tensor, target: torch.Tensor, kernel_size: int,
+                     smooth_dr: float) -> torch.Tensor:
+    return loss_map_backward(grad_map, pred, target, kernel_size, smooth_dr)
+
+
+@_loss_map_bwd_op.register_fake
+def _(grad_map, pred, target, kernel_size, smooth_dr):
+    return torch.empty_like(pred)
 
 
 @torch.library.custom_op("fused_lncc::scale_grad_", mutates_args=("grad",))
@@ -144,14 +216,15 @@ class FusedLNCC(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, pred, target, kernel_size, smooth_dr, need_grad=None):
+    def forward(ctx, pred, target, kernel_size, smooth_dr, need_grad=None, reduction=0):
         # Grad mode is off inside forward; the caller passes whether the graph wants d/dpred.
         if need_grad is None:
             need_grad = bool(ctx.needs_input_grad[0])
-        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr, need_grad)
+        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr, need_grad, reduction)
         ctx.save_for_backward(pred, target)
         ctx.k = kernel_size
         ctx.dr = smooth_dr
+        ctx.reduction = reduction
         ctx.grad = g if need_grad else None
         return loss
 
@@ -161,23 +234,48 @@ class FusedLNCC(torch.autograd.Function):
         ctx.grad = None  # hand the buffer over; a later backward recomputes
         if g is None or g.numel() == 0:
             pred, target = ctx.saved_tensors
-            _, g = torch.ops.fused_lncc.fwd_grad(pred, target, ctx.k, ctx.dr, True)
+            _, g = torch.ops.fused_lncc.fwd_grad(pred, target, ctx.k, ctx.dr, True, ctx.reduction)
         torch.ops.fused_lncc.scale_grad_(g, grad_out)
-        return g, None, None, None, None
+        return g, None, None, None, None, None
 
 
 _FusedLNCC = FusedLNCC  # the reference's private name
 
 
-def fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5):
+class FusedLNCCMap(torch.autograd.Function):
+    """reduction='none': the per-voxel loss map 1 - cc, with the gradient of sum(G * map) for any
+    upstream map G (materialising path: three fp32 adjoint maps weighted by G, then boxed)."""
+
+    @staticmethod
+    def forward(ctx, pred, target, kernel_size, smooth_dr):
+        ctx.save_for_backward(pred, target)
+        ctx.k = kernel_size
+        ctx.dr = smooth_dr
+        return torch.ops.fused_lncc.loss_map(pred, target, kernel_size, smooth_dr)
+
+    @staticmethod
+    def backward(ctx, grad_map):
+        pred, target = ctx.saved_tensors
+        g = torch.ops.fused_lncc.loss_map_backward(grad_map.contiguous(), pred, target, ctx.k, ctx.dr)
+        return g, None, None, None
+
+
+def fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5, reduction="mean"):
     """1 - mean(squared local NCC). Gradient flows through `pred` only.
 
     pred, target: (N, C, D, H, W) fp32 or bf16 CUDA. kernel_size odd (3, 5, 7 or 9).
-    Returns a 0-dim fp32 loss in [0, 1] (reference fused_lncc/__init__.py:77-83)."""
+    Returns a 0-dim fp32 loss in [0, 1] (reference fused_lncc/__init__.py:77-83).
+    reduction (not in the reference, which lists it as open): 'mean' (default, the reference's
+    loss), 'sum' (sum of 1 - cc, 0-dim fp32) or 'none' (fp32 map 1 - cc of pred's shape)."""
     assert pred.dim() == 5 and pred.shape == target.shape, "expect matching (N,C,D,H,W)"
     assert kernel_size % 2 == 1, "kernel_size must be odd"
+    if reduction == "none":
+        return FusedLNCCMap.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr)
+    if reduction not in REDUCTIONS:
+        raise ValueError(f"fused_lncc: reduction must be 'mean', 'sum' or 'none', got {reduction!r}")
     need_grad = bool(pred.requires_grad and torch.is_grad_enabled())
-    return FusedLNCC.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr, need_grad)
+    return FusedLNCC.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr, need_grad,
+                           REDUCTIONS[reduction])
 
 
 from . import compat  # noqa: E402  (registers the reference's fused_lncc::forward/backward ops)

@@ -35,6 +35,8 @@ SIGNATURES = {
         _vp, ctypes.c_size_t, _vp,                   # workspace, bytes, stream
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
+    "lncc_check_abort": (ctypes.c_int, [_vp, _vp]),
+    "lncc_wait_timeout_selftest": (ctypes.c_int, [_vp, ctypes.c_size_t, ctypes.c_uint, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
     "lncc_set_companion": (ctypes.c_int, [ctypes.c_int]),
     "lncc_launch_count": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int, _c_i64,
@@ -47,6 +49,19 @@ SIGNATURES = {
         _vp, ctypes.c_float, _vp,                    # grad, grad_scale, grad_scale_dev
         _vp, _vp, ctypes.c_double,                   # cc_sum_out, loss_out, loss_count
         _vp,                                         # stream
+    ]),
+    "lncc_loss_map_scratch_bytes": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "lncc_loss_map_forward": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int,                      # pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float,                # kernel_size, smooth_dr
+        _vp, _vp,                                    # loss_map, stream
+    ]),
+    "lncc_loss_map_backward": (ctypes.c_int, [
+        _vp, _vp, _vp, ctypes.c_int,                 # grad_map, pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_float,                # kernel_size, smooth_dr
+        _vp, _vp, ctypes.c_size_t, _vp,              # grad, scratch, scratch_bytes, stream
     ]),
     "lncc_maps_forward": (ctypes.c_int, [
         _vp, _vp, ctypes.c_int,                      # pred, target, dtype
@@ -103,13 +118,13 @@ def check(status, what):
         raise RuntimeError(f"{what}: {strerror(status)} (status {status})")
 
 
-KERNEL_AUTO, KERNEL_SWEEP, KERNEL_BAND, KERNEL_WS = 0, 1, 2, 3
+KERNEL_AUTO, KERNEL_SWEEP, KERNEL_WS = 0, 1, 3
 
 
 def select_kernel(which):
     """Process-wide kernel choice: 0 auto (warp-specialised cluster kernel where it applies, else the
-    band kernel, else the general sweep kernel), 1 general sweep kernel, 2 band kernel where supported,
-    3 warp-specialised cluster kernel where supported."""
+    general sweep kernel), 1 general sweep kernel, 3 warp-specialised cluster kernel where supported.
+    2 (an earlier cluster kernel, since retired) is rejected."""
     check(load().lncc_select_kernel(int(which)), "lncc_select_kernel")
 
 

@@ -4,7 +4,12 @@
  * Every entry point is a plain C function: raw device pointers, sizes, a CUDA stream, and an int
  * status code (LNCC_OK == 0). No C++ exception crosses this boundary and no call allocates device
  * memory: the caller owns every buffer, including the scratch "workspace" whose size
- * lncc_workspace_bytes() reports. All work is enqueued on the caller's stream, on the current device.
+ * lncc_workspace_bytes() reports. Work runs on the current device and is ordered on the caller's
+ * stream: everything queued on that stream after a call sees all of its results. One exception to
+ * "only on the caller's stream": for large calls lncc_fused_forward adds a second ("companion")
+ * launch that runs concurrently on a stream the library makes for the calling host thread (with two
+ * events) on its first such call, forked from and joined back into the caller's stream. To keep every
+ * launch on the caller's stream, call lncc_set_companion(0) or use lncc_fused_forward_noalloc.
  *
  * Layout: pred/target/grad are contiguous (B, D, H, W) volumes, B = N*C, W fastest, fp32 or bf16.
  *
@@ -36,7 +41,8 @@ enum lncc_status {
   LNCC_ERR_SMEM = 5,            /* shared memory need above the device opt-in cap (lncc3d.cu:143-148) */
   LNCC_ERR_WORKSPACE = 6,       /* workspace missing or smaller than lncc_workspace_bytes() */
   LNCC_ERR_CUDA = 7,            /* other CUDA runtime error */
-  LNCC_ERR_TOO_LARGE = 8        /* size beyond a stated fixed maximum */
+  LNCC_ERR_TOO_LARGE = 8,       /* size beyond a stated fixed maximum */
+  LNCC_ERR_ABORTED = 9          /* a bounded wait in the kernel timed out (lncc_check_abort) */
 };
 
 /* Element types of pred / target / grad (the reference dispatches on the same two, lncc3d.cu:151-158). */
@@ -49,8 +55,8 @@ const char* lncc_strerror(int status);
 int lncc_version(void);
 
 /*
- * Bytes of scratch the fused kernel needs for a call with these sizes: one fp64 partial sum of cc
- * per thread block. The reference allocates its four fp32 maps itself (lncc3d.cu:130-132); here the
+ * Bytes of scratch the fused kernel needs for a call with these sizes: a 16-byte header (the abort
+ * word read by lncc_check_abort) and one fp64 partial sum of cc per thread block. The reference allocates its four fp32 maps itself (lncc3d.cu:130-132); here the
  * only scratch is this small partials array (a few KB to a few hundred KB).
  * z_begin/z_end: output plane range (see lncc_fused_forward); pass 0, D for whole volumes.
  */
@@ -74,7 +80,11 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
  *   cc_sum_out   : NULL or one device double receiving sum(cc) over the produced voxels.
  *   loss_out     : NULL or one device float receiving 1 - sum(cc)/loss_count.
  *   workspace    : device scratch of at least lncc_workspace_bytes(...) bytes (8-byte aligned).
- * The cc sum is reduced in a fixed order: results are bitwise reproducible run to run.
+ * The cc sum is reduced in a fixed order: for the same launch plan (the same sizes, the same pointer
+ * alignment, and the companion launch either taken or not) results are bitwise reproducible run to
+ * run. Whether the companion runs (lncc_set_companion; inside a stream capture it runs only for a
+ * thread that has made an eager companion-sized call before) changes the last bits of the volumes
+ * it computes.
  */
 int lncc_fused_forward(const void* pred, const void* target, int dtype,
                        int64_t B, int64_t D, int64_t H, int64_t W,
@@ -83,6 +93,23 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype,
                        void* grad, float grad_scale, const float* grad_scale_dev,
                        double* cc_sum_out, float* loss_out, double loss_count,
                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Status of the last lncc_fused_forward call that used `workspace`: LNCC_ERR_ABORTED when one of its
+ * bounded waits (mbarrier waits of the warp-specialised kernel, 2 s each) ran out, in which case its
+ * gradient and loss are invalid (the loss is also NaN), else LNCC_OK. The kernel leaves its loops
+ * and returns after a timeout, so the CUDA context stays usable. Synchronises `stream` and reads
+ * the workspace's first word; call it after that call, on the same stream. No counterpart in the
+ * reference, whose kernels have no waits.
+ */
+int lncc_check_abort(const void* workspace, cudaStream_t stream);
+
+/*
+ * Self-test of the bounded wait: one warp waits on an mbarrier that nothing completes, gives up after
+ * limit_us microseconds (1 .. 10^7) and records the abort in the workspace header exactly as the
+ * fused kernel does, so that lncc_check_abort then returns LNCC_ERR_ABORTED. Diagnostics.
+ */
+int lncc_wait_timeout_selftest(void* workspace, size_t workspace_bytes, unsigned limit_us, cudaStream_t stream);
 
 /*
  * In place grad *= *grad_out for n elements of `dtype`; every block returns at once when
@@ -149,12 +176,29 @@ int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_
                cudaStream_t stream);
 
 /*
+ * Per-voxel loss (reduction 'none'), a feature the reference lists as open (BENCHMARKS.md:177-178)
+ * and has no entry point for. lncc_loss_map_forward writes loss_map = 1 - ncc at every voxel, fp32
+ * (B, D, H, W), with ncc clamped to 1 and NaN kept exactly as in lncc_maps_forward.
+ * lncc_loss_map_backward writes grad = d(sum_v G(v) * loss_map(v))/dpred = -sum_v G(v) dncc(v)/dpred
+ * in pred's dtype for an upstream fp32 (B, D, H, W) map G (grad_map): the adjoints of every voxel are
+ * weighted by G there, then boxed as in lncc_maps_backward. It materialises three fp32 maps in the
+ * caller's scratch of lncc_loss_map_scratch_bytes() bytes (12 bytes per voxel).
+ */
+size_t lncc_loss_map_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W);
+int lncc_loss_map_forward(const void* pred, const void* target, int dtype,
+                          int64_t B, int64_t D, int64_t H, int64_t W,
+                          int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream);
+int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype,
+                           int64_t B, int64_t D, int64_t H, int64_t W,
+                           int kernel_size, float smooth_dr, void* grad,
+                           float* scratch, size_t scratch_bytes, cudaStream_t stream);
+
+/*
  * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:
- * the warp-specialised cluster kernel when W % 4 == 0 and the pointers are 16-byte (fp32) / 8-byte
- * (bf16) aligned, else the cluster "band" kernel when W <= 128, W % 4 == 0, H <= 256 and the
- * pointers are 16-byte aligned, else the general sweep kernel), 1 = always the general sweep
- * kernel, 2 = band kernel where supported, 3 = warp-specialised kernel where supported. No
- * counterpart in the reference, which has a single kernel per step.
+ * the warp-specialised cluster kernel when W % 4 == 0 and the pointers are aligned to 4 elements,
+ * else the general sweep kernel), 1 = always the general sweep kernel, 3 = warp-specialised kernel
+ * where supported. 2 named an earlier cluster kernel that has been retired; it returns
+ * LNCC_ERR_BAD_ARG. No counterpart in the reference, which has a single kernel per step.
  */
 int lncc_select_kernel(int which);
 

@@ -49,7 +49,7 @@ def test_fake_impls_give_fp32_loss_and_pred_dtype_grad():
     from torch._subclasses.fake_tensor import FakeTensorMode
     with FakeTensorMode():
         p = torch.empty(1, 1, 8, 8, 8, dtype=torch.bfloat16)
-        loss, g = torch.ops.fused_lncc.fwd_grad(p, p, 7, 1e-5, True)
+        loss, g = torch.ops.fused_lncc.fwd_grad(p, p, 7, 1e-5, True, 0)
         assert loss.dtype == torch.float32 and loss.dim() == 0
         assert g.dtype == torch.bfloat16 and g.shape == p.shape
 
@@ -81,3 +81,16 @@ def test_compat_checks_raise_runtime_error():
         compat.box3d_sep_forward(x, 3)
     with pytest.raises(RuntimeError):
         compat.lncc_forward(torch.zeros(1, 2, 4, 4, 4), torch.zeros(1, 2, 4, 4, 4), 3, 1e-5)
+
+
+def test_reduction_ops_registered_with_fakes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    assert hasattr(torch.ops.fused_lncc, "loss_map") and hasattr(torch.ops.fused_lncc, "loss_map_backward")
+    with FakeTensorMode():
+        p = torch.empty(1, 1, 8, 8, 8, dtype=torch.bfloat16)
+        m = torch.ops.fused_lncc.loss_map(p, p, 7, 1e-5)
+        assert m.dtype == torch.float32 and m.shape == p.shape
+        g = torch.ops.fused_lncc.loss_map_backward(m, p, p, 7, 1e-5)
+        assert g.dtype == torch.bfloat16 and g.shape == p.shape
+        loss, g2 = torch.ops.fused_lncc.fwd_grad(p, p, 7, 1e-5, True, 1)
+        assert loss.dim() == 0 and g2.shape == p.shape

@@ -274,11 +274,11 @@ def test_plane_range_matches_whole_volume():
     assert abs(parts - s_full.item()) < 1e-6 * max(1.0, abs(s_full.item()))
 
 
-# ---- every kernel: the warp-specialised cluster kernel (default), the band kernel, the general sweep --
-@pytest.fixture(params=["sweep", "band", "ws"])
+# ---- every kernel: the warp-specialised cluster kernel (default) and the general sweep -----------------
+@pytest.fixture(params=["sweep", "ws"])
 def kernel(request):
     from fused_lncc import _lib
-    _lib.select_kernel({"sweep": _lib.KERNEL_SWEEP, "band": _lib.KERNEL_BAND, "ws": _lib.KERNEL_WS}[request.param])
+    _lib.select_kernel({"sweep": _lib.KERNEL_SWEEP, "ws": _lib.KERNEL_WS}[request.param])
     yield request.param
     _lib.select_kernel(_lib.KERNEL_AUTO)
 
@@ -293,11 +293,11 @@ def test_both_kernels_match_oracle(kernel, shape, k):
 
 
 @pytest.mark.parametrize("k", [3, 5, 7, 9])
-def test_band_equals_sweep_blurred(k):
+def test_ws_equals_sweep_blurred(k):
     from fused_lncc import _lib, synth
     pred, target = synth.blurred_pair((2, 2, 48, 64, 128), device="cuda")
     outs = []
-    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_BAND, _lib.KERNEL_WS):
+    for which in (_lib.KERNEL_SWEEP, _lib.KERNEL_WS):
         _lib.select_kernel(which)
         try:
             outs.append(fused(pred, target, k))
@@ -439,7 +439,7 @@ def test_ws_companion_under_graph_capture():
     del graph
 
 
-def test_band_bf16_and_loss_only():
+def test_bf16_k9_and_loss_only():
     from fused_lncc import synth
     pred, target = synth.blurred_pair((2, 2, 40, 64, 64), device="cuda", dtype=torch.bfloat16)
     lb, gb = fused(pred, target, 9)
@@ -449,3 +449,26 @@ def test_band_bf16_and_loss_only():
     assert gb.dtype == torch.bfloat16 and rel < BF16_REL
     with torch.no_grad():
         assert abs(fused_lncc_loss(pred, target, 9).item() - lb) < 1e-7
+
+
+def test_wait_timeout_is_reported_as_status():
+    """A bounded wait that runs out is recorded in the workspace and read back as LNCC_ERR_ABORTED;
+    the context stays usable, and a normal call afterwards clears the record."""
+    from fused_lncc import _lib, synth
+    lib = _lib.load()
+    ws = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.lncc_wait_timeout_selftest(ws.data_ptr(), ws.numel(), 20000, stream) == 0
+    assert lib.lncc_check_abort(ws.data_ptr(), stream) == 9  # LNCC_ERR_ABORTED
+    pred, target = synth.blurred_pair((1, 2, 24, 32, 64), device="cuda")
+    B, D, H, W = 2, 24, 32, 64
+    nb = lib.lncc_workspace_bytes(B, D, H, W, 7, 0, 0, D)
+    ws2 = torch.full((nb,), 0xFF, dtype=torch.uint8, device="cuda")  # garbage header
+    g = torch.empty_like(pred)
+    st = lib.lncc_fused_forward(pred.data_ptr(), target.data_ptr(), 0, B, D, H, W, 7, 1e-5, 0, D, g.data_ptr(),
+                                1.0, None, None, None, 1.0, ws2.data_ptr(), nb, stream)
+    assert st == 0
+    assert lib.lncc_check_abort(ws2.data_ptr(), stream) == 0
+    lf, _ = fused(pred, target, 7)
+    lo, _ = oracle(pred, target, 7)
+    assert abs(lf - lo) < FP32_LOSS_TOL
