@@ -2,6 +2,10 @@
 
 Usage: python fused-lncc_b200/build.py [--force] [--checked]
 
+--checked builds the bounds-checked variant (LNCC_CHECKED=1) into liblncc_sm100_checked.so beside
+the product library: every kernel access is range-checked and entry points report violations as
+LNCC_ERR_CHECK (include/lncc.h, lncc_checked_build).
+
 The reference builds a pybind torch extension for sm_70..sm_120 without sm_100
 (reference setup.py:16-23,42-49). This builds a plain shared library for sm_100a only, with -O3
 and -lineinfo and, like the reference, without --use_fast_math (the variance terms
@@ -20,6 +24,7 @@ INCLUDE = os.path.join(REPO_ROOT, "include")
 LIB_DIR = os.path.join(PKG_ROOT, "fused_lncc")
 LIB_NAME = "liblncc_sm100.so"
 LIB_PATH = os.path.join(LIB_DIR, LIB_NAME)
+CHECKED_LIB_PATH = os.path.join(LIB_DIR, "liblncc_sm100_checked.so")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -44,7 +49,7 @@ def _stale(out):
 
 def build_library(force=False, checked=False, verbose=False, out=None):
     """Compile the library if it is missing or older than its sources; return its path."""
-    out = out or LIB_PATH
+    out = out or (CHECKED_LIB_PATH if checked else LIB_PATH)
     if not force and not _stale(out):
         return out
     cmd = [nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-I", INCLUDE,

@@ -40,6 +40,7 @@ struct Args {
   void* out[4];        // MAPS: ncc, A, Bc, Cc (fp32, each may be null); BWD: grad (S); BOX: y (fp32)
   const float* wmap;   // MAPS: null, or a (B, D, H, W) fp32 map multiplying A, Bc, Cc voxel by voxel
   int loss_map;        // MAPS: out[0] receives 1 - ncc instead of ncc
+  int64_t n_elems;     // B * D * H * W (range checks of the checked build)
   int D, H, W;
   int tiles_x, tiles_y, chunks;
   float n, ndr, scale;
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
     const int64_t zo = vol + int64_t(z) * HW;
 #pragma unroll
     for (int j = 0; j < PPT; ++j) {
-      if (!in[j]) continue;
+      if (!in[j] || !LNCC_IN(zo + off[j], 1, a.n_elems)) continue;
       if (MODE == MAPS) {
         const float p = ld(static_cast<const S*>(a.in[0]) + zo + off[j]);
         const float t = ld(static_cast<const S*>(a.in[1]) + zo + off[j]);
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
 #pragma unroll
     for (int j = 0; j < PPT; ++j) {
       const int i = tid + j * NT;
-      if (i < FP) {
+      if (i < FP && LNCC_IN(i, 1, FH * FW)) {
 #pragma unroll
         for (int f = 0; f < NF; ++f) DS[f][i / FW][i % FW] = s[j][f];
       }
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
         float h = 0.f;
 #pragma unroll
         for (int d = 0; d < K; ++d) h += DS[f][r + d][c];
-        HS[f][r][c] = h;
+        if (LNCC_IN((r + K - 1) * FW + c, 1, FH * FW) && LNCC_IN(r * FW + c, 1, TH * FW)) HS[f][r][c] = h;
       }
     }
     __syncthreads();
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
         w[f] = h;
       }
       const int64_t o = vol + int64_t(z) * HW + int64_t(y) * a.W + x;
+      if (!LNCC_IN(o, 1, a.n_elems) || !LNCC_IN(r * FW + c + K - 1, 1, TH * FW)) continue;
       if (MODE == MAPS) {
         // n-scaled statistics (X = n*cross, VP = n*var_p, VT = n*var_t): the same cancellation of
         // constant inputs as the reference's division by n, and the same maps:

@@ -24,6 +24,7 @@
 //   Cc = 2n*c, Bc = -n*b, A = -2*a  for  c = w, b = w*w*VT, a = w*(St - w*VT*Sp),
 // and d(sum cc)/dp = box(A) + 2p*box(Bc) + t*box(Cc) = 2*(n*t*box(c) - n*p*box(b) - box(a)).
 #include "lncc.h"
+#include "lncc_check.cuh"
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -90,6 +91,7 @@ struct SweepArgs {
   int z_begin, z_end, dchunk;
   int tiles_w, tiles_h, nchunks;
   unsigned* abort_word;  // workspace word that lncc_check_abort reads; this kernel never waits, so it only clears it
+  int64_t n_in, n_g, n_parts;  // elements of p / t, of g, and partials (range checks of the checked build)
 };
 
 template <int R, int TH, int TW, int NT, typename S, bool GRAD>
@@ -157,7 +159,7 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
     for (int i = 0; i < PPT; ++i) {
       np_[i] = 0.f;
       nt_[i] = 0.f;
-      if (pv && aval[i]) {
+      if (pv && aval[i] && LNCC_IN(b * D * HW + int64_t(j) * HW + aoff[i], 1, a.n_in)) {
         np_[i] = ldf<S>(P + int64_t(j) * HW + aoff[i]);
         nt_[i] = ldf<S>(T + int64_t(j) * HW + aoff[i]);
       }
@@ -189,10 +191,13 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
         s5[i][2] = fmaf(p, p, fmaf(-op, op, s5[i][2]));
         s5[i][3] = fmaf(t, t, fmaf(-ot, ot, s5[i][3]));
         s5[i][4] = fmaf(p, t, fmaf(-op, ot, s5[i][4]));
-        ring[(slot * 2 + 0) * F0 + q] = p;
-        ring[(slot * 2 + 1) * F0 + q] = t;
+        if (LNCC_IN((slot * 2 + 1) * F0 + q, 1, K * 2 * F0)) {
+          ring[(slot * 2 + 0) * F0 + q] = p;
+          ring[(slot * 2 + 1) * F0 + q] = t;
+        }
 #pragma unroll
-        for (int f = 0; f < 5; ++f) DS[f * F0 + q] = s5[i][f];
+        for (int f = 0; f < 5; ++f)
+          if (LNCC_IN(f * F0 + q, 1, 5 * F0)) DS[f * F0 + q] = s5[i][f];
       }
     }
     if (j + 1 < j1) load_plane(j + 1);
@@ -212,10 +217,11 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
         float s = 0.f;
 #pragma unroll
         for (int d = 0; d < 2 * R + 1; ++d) s += src[d * W0];
-        dst[0] = s;
+        if (LNCC_IN(f * H1 * W0 + c, 1, 5 * H1 * W0)) dst[0] = s;
         for (int r = 1; r < H1; ++r) {
+          if (!LNCC_IN(f * F0 + (r + 2 * R) * W0 + c, 1, 5 * F0)) break;
           s += src[(r + 2 * R) * W0] - src[(r - 1) * W0];
-          dst[r * W0] = s;
+          if (LNCC_IN(f * H1 * W0 + r * W0 + c, 1, 5 * H1 * W0)) dst[r * W0] = s;
         }
       }
     }
@@ -260,9 +266,11 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
             const float wv = w * VT;
             const float bq = w * wv;
             const float aq = w * fmaf(-wv, Sp, St);
-            ADJ[0 * F1 + r * W1 + c] = live ? aq : 0.f;
-            ADJ[1 * F1 + r * W1 + c] = live ? bq : 0.f;
-            ADJ[2 * F1 + r * W1 + c] = live ? w : 0.f;
+            if (LNCC_IN(2 * F1 + r * W1 + c, 1, 3 * F1) && LNCC_IN(r * W1 + c, 1, F1)) {
+              ADJ[0 * F1 + r * W1 + c] = live ? aq : 0.f;
+              ADJ[1 * F1 + r * W1 + c] = live ? bq : 0.f;
+              ADJ[2 * F1 + r * W1 + c] = live ? w : 0.f;
+            }
           }
         }
       }
@@ -286,11 +294,12 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
         float s = 0.f;
 #pragma unroll
         for (int d = 0; d < 2 * R + 1; ++d) s += src[(r0 + d) * W1];
-        dst[r0 * W1] = s;
+        if (LNCC_IN(f * TH * W1 + r0 * W1 + c, 1, 3 * TH * W1)) dst[r0 * W1] = s;
 #pragma unroll
         for (int r = r0 + 1; r < r0 + LH; ++r) {
           s += src[(r + 2 * R) * W1] - src[(r - 1) * W1];
-          dst[r * W1] = s;
+          if (LNCC_IN(f * F1 + (r + 2 * R) * W1 + c, 1, 3 * F1) && LNCC_IN(f * TH * W1 + r * W1 + c, 1, 3 * TH * W1))
+            dst[r * W1] = s;
         }
       }
     }
@@ -315,8 +324,10 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
             for (int d = 0; d < 2 * R + 1; ++d) s += src[d];
             v[f] = s;
             float* rs = ring2 + (slot2 * 3 + f) * F2 + q;
-            T3[e][f] += s - *rs;
-            *rs = s;
+            if (LNCC_IN((slot2 * 3 + f) * F2 + q, 1, K * 3 * F2)) {
+              T3[e][f] += s - *rs;
+              *rs = s;
+            }
           }
           const int gy = y0 + r, gx = x0 + c;
           if (c2_out && gy < H && gx < W) {
@@ -324,7 +335,9 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
             const float p = ring[(pslot * 2 + 0) * F0 + q0];
             const float t = ring[(pslot * 2 + 1) * F0 + q0];
             const float gval = gs * fmaf(nf, fmaf(t, T3[e][2], -p * T3[e][1]), -T3[e][0]);
-            stg<S>(G + int64_t(c2 - a.z_begin) * HW + gy * W + gx, gval);
+            if (LNCC_IN(b * int64_t(a.z_end - a.z_begin) * HW + int64_t(c2 - a.z_begin) * HW + gy * W + gx, 1, a.n_g) &&
+                LNCC_IN((pslot * 2 + 1) * F0 + q0, 1, K * 2 * F0))
+              stg<S>(G + int64_t(c2 - a.z_begin) * HW + gy * W + gx, gval);
           }
         }
       }
@@ -341,7 +354,7 @@ __global__ void __launch_bounds__(NT) lncc_sweep_kernel(const SweepArgs a) {
   if (tid == 0) {
     double s = 0.0;
     for (int w = 0; w < NT / 32; ++w) s += red[w];
-    a.partials[blockIdx.x] = s;
+    if (LNCC_IN(blockIdx.x, 1, a.n_parts)) a.partials[blockIdx.x] = s;
   }
 }
 
@@ -499,15 +512,24 @@ static int ws_chunk(int64_t W, int dtype, const void* p, const void* t, const vo
 }
 
 template <int R, typename S, bool GRAD, int CW, bool ASSIST>
+static auto ws_kernel_ptr() {
+  return ws::lncc_ws_kernel<R, S, GRAD, CW, ASSIST>;
+}
+template <int R>
+static constexpr int ws_smem_r() {
+  return ws::smem_bytes<R>();
+}
+
+template <int R, typename S, bool GRAD, int CW, bool ASSIST>
 static cudaError_t ws_prepare(const void** fn_out) {
-  auto kfn = ws::lncc_ws_kernel<R, S, GRAD, CW, ASSIST>;
+  auto kfn = ws_kernel_ptr<R, S, GRAD, CW, ASSIST>();
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
   if (!bit || !(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, ws::smem_bytes<R>());
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem_r<R>());
     if (e != cudaSuccess) return e;
     // clusters of up to 16 CTAs (tall planes); the occupancy query then reports how many fit
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
@@ -544,10 +566,10 @@ static cudaError_t ws_kernel_fn(int R, int dtype, bool grad, int cw, bool assist
 
 static int ws_smem_for(int R) {
   switch (R) {
-    case 1: return ws::smem_bytes<1>();
-    case 2: return ws::smem_bytes<2>();
-    case 3: return ws::smem_bytes<3>();
-    default: return ws::smem_bytes<4>();
+    case 1: return ws_smem_r<1>();
+    case 2: return ws_smem_r<2>();
+    case 3: return ws_smem_r<3>();
+    default: return ws_smem_r<4>();
   }
 }
 
@@ -769,6 +791,7 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
     a1.items_per_cluster = (a1.total_items + wp.nclusters - 1) / wp.nclusters;
     const int64_t nc = (a1.total_items + a1.items_per_cluster - 1) / a1.items_per_cluster;
     *nparts = int64_t(wp.cy) * nc;
+    a1.n_parts = *nparts;
     return launch_ws_grid(wp, wp.cy, nc, a1, st);
   }
   *nparts = wp.parts();
@@ -778,13 +801,22 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
     const int zs = wa.z_end - int(wp.z2);
     a1.z_end = zs;
     a2.z_begin = zs;
-    if (wa.g) a2.g = static_cast<char*>(wa.g) + size_t(int64_t(zs - wa.z_begin) * H * W) * esz;
+    if (wa.g) {
+      a2.g = static_cast<char*>(wa.g) + size_t(int64_t(zs - wa.z_begin) * H * W) * esz;
+      a2.n_g = wa.n_g - int64_t(zs - wa.z_begin) * H * W;
+    }
   } else {  // the main launch takes volumes [0, B - b2), the companion the rest
     const int64_t b1 = B - wp.b2;
     a2.p = static_cast<const char*>(wa.p) + size_t(b1 * D * H * W) * esz;
     a2.t = static_cast<const char*>(wa.t) + size_t(b1 * D * H * W) * esz;
-    if (wa.g) a2.g = static_cast<char*>(wa.g) + size_t(b1 * (int64_t(wa.z_end) - wa.z_begin) * H * W) * esz;
+    a2.n_in = wp.b2 * D * H * W;
+    if (wa.g) {
+      a2.g = static_cast<char*>(wa.g) + size_t(b1 * (int64_t(wa.z_end) - wa.z_begin) * H * W) * esz;
+      a2.n_g = wp.b2 * (int64_t(wa.z_end) - wa.z_begin) * H * W;
+    }
   }
+  a1.n_parts = int64_t(wp.cy) * wp.nclusters;
+  a2.n_parts = int64_t(WsPlan::kCompanionCy) * wp.nclusters2;
   cudaError_t e = cudaEventRecord(fork, st);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, fork, 0);
   if (e == cudaSuccess) e = launch_ws_grid(wp, wp.cy, wp.nclusters, a1, st);
@@ -847,6 +879,7 @@ static int compat_plan(int64_t B, int64_t D, int64_t H, int64_t W, int k, compat
   if (!valid_k(k)) return LNCC_ERR_KERNEL_SIZE;
   if (B < 1 || D < 1 || H < 1 || W < 1) return LNCC_ERR_BAD_ARG;
   if (D > INT32_MAX / 2 || H > INT32_MAX / 2 || W > INT32_MAX / 2) return LNCC_ERR_TOO_LARGE;
+  a->n_elems = B * D * H * W;
   a->D = int(D);
   a->H = int(H);
   a->W = int(W);
@@ -859,6 +892,28 @@ static int compat_plan(int64_t B, int64_t D, int64_t H, int64_t W, int k, compat
   *nblocks = nb;
   return LNCC_OK;
 }
+
+// ---- checked build: every entry point reports range violations of its launches ----------------------
+#ifdef LNCC_CHECKED
+static int check_begin() {
+  const unsigned long long z = 0;
+  return cudaMemcpyToSymbol(g_check_violations, &z, sizeof(z)) == cudaSuccess ? LNCC_OK : LNCC_ERR_CUDA;
+}
+static int check_end(int status, cudaStream_t st) {
+  if (status != LNCC_OK) return status;
+  unsigned long long n = 0;
+  if (cudaStreamSynchronize(st) != cudaSuccess ||
+      cudaMemcpyFromSymbol(&n, g_check_violations, sizeof(n)) != cudaSuccess)
+    return LNCC_ERR_CUDA;
+  return n ? LNCC_ERR_CHECK : LNCC_OK;
+}
+#define LNCC_CHECKED_ENTRY(body, stream)   \
+  do {                                     \
+    const int cb_ = check_begin();         \
+    if (cb_ != LNCC_OK) return cb_;        \
+    return check_end((body), (stream));    \
+  } while (0)
+#endif
 
 }  // namespace lncc
 
@@ -878,6 +933,7 @@ const char* lncc_strerror(int status) {
     case LNCC_ERR_CUDA: return "fused_lncc: CUDA runtime error";
     case LNCC_ERR_TOO_LARGE: return "fused_lncc: size exceeds the fixed maximum of this entry point";
     case LNCC_ERR_ABORTED: return "fused_lncc: a bounded wait in the kernel timed out; the results of that call are invalid";
+    case LNCC_ERR_CHECK: return "fused_lncc: checked build: a kernel index left its array (the access was skipped)";
     default: return "fused_lncc: unknown status";
   }
 }
@@ -899,7 +955,7 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
   return need + kWsHeader;
 }
 
-int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+static int impl_lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                        int64_t W, int kernel_size, float smooth_dr, int64_t z_begin, int64_t z_end,
                        void* grad, float grad_scale, const float* grad_scale_dev, double* cc_sum_out,
                        float* loss_out, double loss_count, void* workspace, size_t workspace_bytes,
@@ -933,6 +989,9 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
   a.g = grad;
   a.partials = reinterpret_cast<double*>(static_cast<char*>(workspace) + kWsHeader);
   a.abort_word = static_cast<unsigned*>(workspace);
+  a.n_in = B * D * H * W;
+  a.n_g = grad ? B * (z_end - z_begin) * H * W : 0;
+  a.n_parts = nparts;
   a.gscale_dev = grad_scale_dev;
   a.gscale = grad_scale;
   a.n = float(kernel_size * kernel_size * kernel_size);
@@ -957,6 +1016,9 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t 
     wa.partials = a.partials;
     wa.abort_word = a.abort_word;
     wa.clear_abort = 1;
+    wa.n_in = B * D * H * W;
+    wa.n_g = grad ? B * (z_end - z_begin) * H * W : 0;
+    wa.n_parts = nparts;
     wa.gscale_dev = grad_scale_dev;
     wa.gscale = grad_scale;
     wa.n = a.n;
@@ -1011,6 +1073,14 @@ int lncc_fused_forward_noalloc(const void* pred, const void* target, int dtype, 
   return r == LNCC_ERR_WORKSPACE ? LNCC_ERR_TOO_LARGE : r;
 }
 
+int lncc_checked_build(void) {
+#ifdef LNCC_CHECKED
+  return 1;
+#else
+  return 0;
+#endif
+}
+
 int lncc_check_abort(const void* workspace, cudaStream_t stream) {
   if (!workspace || (uintptr_t(workspace) % 8)) return LNCC_ERR_BAD_ARG;
   unsigned w = 0;
@@ -1046,7 +1116,7 @@ int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_siz
   return (wp.ok && (wp.b2 > 0 || wp.z2 > 0)) ? 2 : 1;
 }
 
-int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+static int impl_lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                       int64_t W, int kernel_size, float smooth_dr, float* ncc, float* A, float* Bc, float* Cc,
                       cudaStream_t stream) {
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
@@ -1072,7 +1142,7 @@ int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
-int lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const void* pred, const void* target,
+static int impl_lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const void* pred, const void* target,
                        int dtype, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, float scale,
                        void* grad, cudaStream_t stream) {
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
@@ -1096,7 +1166,7 @@ int lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const v
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
-int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size,
+static int impl_lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size,
                cudaStream_t stream) {
   compat::Args a = {};
   int64_t nb = 0;
@@ -1114,7 +1184,7 @@ size_t lncc_loss_map_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W) {
   return size_t(3) * size_t(B) * size_t(D) * size_t(H) * size_t(W) * sizeof(float);
 }
 
-int lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+static int impl_lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                           int64_t W, int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream) {
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
   compat::Args a = {};
@@ -1134,7 +1204,7 @@ int lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
-int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
+static int impl_lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
                            int64_t D, int64_t H, int64_t W, int kernel_size, float smooth_dr, void* grad,
                            float* scratch, size_t scratch_bytes, cudaStream_t stream) {
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
@@ -1179,7 +1249,7 @@ int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* 
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
-int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {
+static int impl_lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {
   if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
   if (!grad || !grad_out_dev || n < 0) return LNCC_ERR_BAD_ARG;
   if (n == 0) return LNCC_OK;
@@ -1194,6 +1264,86 @@ int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev,
     lncc_scale_grad_kernel<__nv_bfloat16><<<unsigned(blocks), threads, 0, stream>>>(
         reinterpret_cast<__nv_bfloat16*>(grad), n, grad_out_dev);
   return cudaGetLastError() == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+// ---- entry points (a checked build adds its range-violation report around each) ------------------
+int lncc_fused_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                       int64_t W, int kernel_size, float smooth_dr, int64_t z_begin, int64_t z_end,
+                       void* grad, float grad_scale, const float* grad_scale_dev, double* cc_sum_out,
+                       float* loss_out, double loss_count, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_fused_forward(
+      pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, z_begin, z_end, grad, grad_scale,
+      grad_scale_dev, cc_sum_out, loss_out, loss_count, workspace, workspace_bytes, stream), stream);
+#else
+  return impl_lncc_fused_forward(
+      pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, z_begin, z_end, grad, grad_scale,
+      grad_scale_dev, cc_sum_out, loss_out, loss_count, workspace, workspace_bytes, stream);
+#endif
+}
+
+int lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                      int64_t W, int kernel_size, float smooth_dr, float* ncc, float* A, float* Bc, float* Cc,
+                      cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_maps_forward(
+      pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, ncc, A, Bc, Cc, stream), stream);
+#else
+  return impl_lncc_maps_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, ncc, A, Bc, Cc, stream);
+#endif
+}
+
+int lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const void* pred, const void* target,
+                       int dtype, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, float scale,
+                       void* grad, cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_maps_backward(
+      A, Bc, Cc, pred, target, dtype, B, D, H, W, kernel_size, scale, grad, stream), stream);
+#else
+  return impl_lncc_maps_backward(A, Bc, Cc, pred, target, dtype, B, D, H, W, kernel_size, scale, grad, stream);
+#endif
+}
+
+int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size,
+               cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_box3d(x, y, B, D, H, W, kernel_size, stream), stream);
+#else
+  return impl_lncc_box3d(x, y, B, D, H, W, kernel_size, stream);
+#endif
+}
+
+int lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                          int64_t W, int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_loss_map_forward(
+      pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, loss_map, stream), stream);
+#else
+  return impl_lncc_loss_map_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, loss_map, stream);
+#endif
+}
+
+int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
+                           int64_t D, int64_t H, int64_t W, int kernel_size, float smooth_dr, void* grad,
+                           float* scratch, size_t scratch_bytes, cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_loss_map_backward(
+      grad_map, pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, grad, scratch, scratch_bytes,
+      stream), stream);
+#else
+  return impl_lncc_loss_map_backward(
+      grad_map, pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, grad, scratch, scratch_bytes,
+      stream);
+#endif
+}
+
+int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {
+#ifdef LNCC_CHECKED
+  LNCC_CHECKED_ENTRY(impl_lncc_scale_grad(grad, dtype, n, grad_out_dev, stream), stream);
+#else
+  return impl_lncc_scale_grad(grad, dtype, n, grad_out_dev, stream);
+#endif
 }
 
 }  // extern "C"

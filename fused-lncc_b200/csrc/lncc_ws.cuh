@@ -39,6 +39,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "lncc_check.cuh"
+
 namespace lncc {
 namespace ws {
 
@@ -70,6 +72,9 @@ struct Args {
   int64_t items_per_cluster;
   unsigned* abort_word;       // workspace word: set to 1 by a CTA whose bounded wait ran out
   int clear_abort;            // this launch's first CTA zeroes abort_word at its start
+  int64_t n_in;               // elements readable from p and t (range checks of the checked build)
+  int64_t n_g;                // elements writable at g
+  int64_t n_parts;            // partials writable at partials
 };
 
 template <int R>
@@ -230,6 +235,7 @@ __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t a, uint32_t 
 // signalled on the destination CTA's barrier `mbar_cluster` (complete_tx). Addresses 16-B aligned.
 __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
                                                   uint32_t mbar_cluster) {
+  if (!LNCC_IN_SMEM(src_cta, bytes)) return;
   asm volatile(
       "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_cluster),
       "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
@@ -273,7 +279,14 @@ __device__ __forceinline__ void mbar_wait(uint32_t a, uint32_t parity, volatile 
 }
 
 // ---- TMEM, used as per-thread storage (lane = thread of the warp quadrant) ------------------------------
+// TMEM column ranges are warp-uniform, so a checked build skips a bad access for the whole warp.
+#define LNCC_TM_OK(ta, n) LNCC_IN((ta) & 0xffffu, n, TMEM_COLS)
 __device__ __forceinline__ void tm_ld16(uint32_t ta, float (&v)[16]) {
+  if (!LNCC_TM_OK(ta, 16)) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    return;
+  }
   uint32_t u[16];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -291,6 +304,7 @@ __device__ __forceinline__ void tm_ld16(uint32_t ta, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(u[i]);
 }
 __device__ __forceinline__ void tm_st16(uint32_t ta, const float (&v)[16]) {
+  if (!LNCC_TM_OK(ta, 16)) return;
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(ta),
       "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
@@ -304,6 +318,11 @@ __device__ __forceinline__ void tm_st16(uint32_t ta, const float (&v)[16]) {
 __device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 16-column load without the wait; the registers are valid only after tm_wait_ld16 names them.
 __device__ __forceinline__ void tm_ld16_issue(uint32_t ta, uint32_t (&u)[16]) {
+  if (!LNCC_TM_OK(ta, 16)) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) u[i] = 0u;
+    return;
+  }
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
@@ -318,17 +337,20 @@ __device__ __forceinline__ void tm_wait_ld16(uint32_t (&u)[16]) {
                  "+r"(u[14]), "+r"(u[15]));
 }
 __device__ __forceinline__ void tm_st8(uint32_t ta, const uint32_t (&u)[8]) {
+  if (!LNCC_TM_OK(ta, 8)) return;
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta), "r"(u[0]),
                "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
                : "memory");
 }
 __device__ __forceinline__ void tm_st4(uint32_t ta, float4 v) {
+  if (!LNCC_TM_OK(ta, 4)) return;
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ta), "r"(__float_as_uint(v.x)),
                "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)), "r"(__float_as_uint(v.w))
                : "memory");
 }
 
 __device__ __forceinline__ void sts4(uint32_t addr, float4 v) {
+  if (!LNCC_IN_SMEM(addr, 16)) return;
   asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
@@ -511,6 +533,16 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
     const int c0 = sg.zs - R;
     const S* __restrict__ P = reinterpret_cast<const S*>(a.p) + sg.b * D * HW;
     const S* __restrict__ T = reinterpret_cast<const S*>(a.t) + sg.b * D * HW;
+    const int64_t vofs = sg.b * D * HW;  // element offset of P and T from a.p and a.t
+    // CW elements of the volume at element offset e (P/T relative); a checked build reads zeros outside
+    auto gld = [&](const S* base, int64_t e, float4* o) {
+      if (LNCC_IN(vofs + e, CW, a.n_in)) {
+        Chunk<S, CW>::ld(base + e, o);
+      } else {
+#pragma unroll
+        for (int h = 0; h < CW / 4; ++h) o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
 
     // D warp's share of the W box of step st (fields 3 and 4 of the paired A warp's sums, same TMEM
     // lanes, same DW rows), once the buffer is free and the sums are complete; false after an abort.
@@ -574,15 +606,15 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         for (int j = 0; j < NCH; ++j) {
           const bool cj = (cm >> j) & 1u;
           if (in_ok && cj) {
-            Chunk<S, CW>::ld(P + zi * HW + roff + CW * j, &r.pi[Q * j]);
-            Chunk<S, CW>::ld(T + zi * HW + roff + CW * j, &r.ti[Q * j]);
+            gld(P, zi * HW + roff + CW * j, &r.pi[Q * j]);
+            gld(T, zi * HW + roff + CW * j, &r.ti[Q * j]);
           } else {
 #pragma unroll
             for (int h = 0; h < Q; ++h) r.pi[Q * j + h] = r.ti[Q * j + h] = z4;
           }
           if (out_ok && cj) {
-            Chunk<S, CW>::ld(P + zo * HW + roff + CW * j, &r.po[Q * j]);
-            Chunk<S, CW>::ld(T + zo * HW + roff + CW * j, &r.to[Q * j]);
+            gld(P, zo * HW + roff + CW * j, &r.po[Q * j]);
+            gld(T, zo * HW + roff + CW * j, &r.to[Q * j]);
           } else {
 #pragma unroll
             for (int h = 0; h < Q; ++h) r.po[Q * j + h] = r.to[Q * j + h] = z4;
@@ -722,13 +754,15 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           // only after this CTA's step-s buffer was released.
           const int r0 = 4 * warp, r1 = 4 * warp + 4;  // this warp's rows
           constexpr uint32_t kRowBytes = 5 * SPAN * 4;
-          if (has_up && r0 < 2 * R) {
+          if (has_up && r0 < 2 * R && LNCC_IN_SMEM(smem_addr(&sm.dw[i][TY + 2 * R + r0][0][0]), uint32_t((r1 < 2 * R ? r1 : 2 * R) - r0) * kRowBytes)) {
             const int e1 = r1 < 2 * R ? r1 : 2 * R;
             bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][TY + 2 * R + r0][0][0]), uint32_t(rank - 1)),
                               smem_addr(&sm.dw[i][2 * R + r0][0][0]), uint32_t(e1 - r0) * kRowBytes,
                               mapa_rank(bar(BAR_DW_FULL, i), uint32_t(rank - 1)));
           }
-          if (has_dn && r1 > TY - 2 * R) {
+          if (has_dn && r1 > TY - 2 * R &&
+              LNCC_IN_SMEM(smem_addr(&sm.dw[i][(r0 > TY - 2 * R ? r0 : TY - 2 * R) - (TY - 2 * R)][0][0]),
+                           uint32_t(r1 - (r0 > TY - 2 * R ? r0 : TY - 2 * R)) * kRowBytes)) {
             const int b0 = r0 > TY - 2 * R ? r0 : TY - 2 * R;
             bulk_copy_to_peer(mapa_rank(smem_addr(&sm.dw[i][b0 - (TY - 2 * R)][0][0]), uint32_t(rank + 1)),
                               smem_addr(&sm.dw[i][2 * R + b0][0][0]), uint32_t(r1 - b0) * kRowBytes,
@@ -797,9 +831,10 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           float cc_acc = 0.f;
 #pragma unroll
           for (int e = 0; e < ERH; ++e) {
-            const float2 v01 = make_float2(dwp[(e * 5 + 0) * SPAN], dwp[(e * 5 + 1) * SPAN]);
-            const float2 v23 = make_float2(dwp[(e * 5 + 2) * SPAN], dwp[(e * 5 + 3) * SPAN]);
-            const float v4 = dwp[(e * 5 + 4) * SPAN];
+            auto lds = [&](int off) -> float { return LNCC_IN_SMEM_PTR(dwp + off, 4) ? dwp[off] : 0.f; };
+            const float2 v01 = make_float2(lds((e * 5 + 0) * SPAN), lds((e * 5 + 1) * SPAN));
+            const float2 v23 = make_float2(lds((e * 5 + 2) * SPAN), lds((e * 5 + 3) * SPAN));
+            const float v4 = lds((e * 5 + 4) * SPAN);
             if (e >= K) {
               s01 = add2(s01, sub2(v01, win01[e % K]));
               s23 = add2(s23, sub2(v23, win23[e % K]));
@@ -847,9 +882,9 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
                 awc[k % K] = cq;
                 if (k >= 2 * R) {
                   const int yo = HR * h + k - 2 * R;
-                  sm.ah[i][0][yo][px] = aab.x;
-                  sm.ah[i][1][yo][px] = aab.y;
-                  sm.ah[i][2][yo][px] = ac;
+                  if (LNCC_IN_SMEM_PTR(&sm.ah[i][0][yo][px], 4)) sm.ah[i][0][yo][px] = aab.x;
+                  if (LNCC_IN_SMEM_PTR(&sm.ah[i][1][yo][px], 4)) sm.ah[i][1][yo][px] = aab.y;
+                  if (LNCC_IN_SMEM_PTR(&sm.ah[i][2][yo][px], 4)) sm.ah[i][2][yo][px] = ac;
                 }
               }
             }
@@ -885,7 +920,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         float v[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float4 w4 = *reinterpret_cast<const float4*>(&sm.ah[i][f][yl][swz_chunk(4 * q + j)]);
+          const float* ahp = &sm.ah[i][f][yl][swz_chunk(4 * q + j)];
+          const float4 w4 = LNCC_IN_SMEM_PTR(ahp, 16) ? *reinterpret_cast<const float4*>(ahp) : make_float4(0.f, 0.f, 0.f, 0.f);
           v[4 * j] = w4.x;
           v[4 * j + 1] = w4.y;
           v[4 * j + 2] = w4.z;
@@ -927,8 +963,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           for (int j = 0; j < NCH; ++j) {
             constexpr int Q = CW / 4;
             if (out_ok && ((om >> j) & 1u)) {
-              Chunk<S, CW>::ld(P + o * HW + roff + CW * j, &pv[Q * j]);
-              Chunk<S, CW>::ld(T + o * HW + roff + CW * j, &tv[Q * j]);
+              gld(P, o * HW + roff + CW * j, &pv[Q * j]);
+              gld(T, o * HW + roff + CW * j, &tv[Q * j]);
             } else {
 #pragma unroll
               for (int h = 0; h < Q; ++h) pv[Q * j + h] = tv[Q * j + h] = z4;
@@ -990,7 +1026,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
                   const int c4 = Q * j + h;
                   g4[h] = grad4(pv[c4], tv[c4], sa + 4 * c4, sb + 4 * c4, sc + 4 * c4);
                 }
-                Chunk<S, CW>::st(gp + CW * j, g4);
+                if (LNCC_IN((gp - reinterpret_cast<S*>(a.g)) + CW * j, CW, a.n_g)) Chunk<S, CW>::st(gp + CW * j, g4);
               }
             }
           }
@@ -1050,14 +1086,14 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
               if (!((om >> j) & 1u)) continue;
               constexpr int Q = CW / 4;
               float4 p4[Q], t4[Q], g4[Q];
-              Chunk<S, CW>::ld(P + o * HW + roff + CW * j, p4);
-              Chunk<S, CW>::ld(T + o * HW + roff + CW * j, t4);
+              gld(P, o * HW + roff + CW * j, p4);
+              gld(T, o * HW + roff + CW * j, t4);
 #pragma unroll
               for (int h = 0; h < Q; ++h) {
                 const int c4 = Q * j + h;
                 g4[h] = grad4(p4[h], t4[h], sum[0] + 4 * c4, sum[1] + 4 * c4, sum[2] + 4 * c4);
               }
-              Chunk<S, CW>::st(gp + CW * j, g4);
+              if (LNCC_IN((gp - reinterpret_cast<S*>(a.g)) + CW * j, CW, a.n_g)) Chunk<S, CW>::st(gp + CW * j, g4);
             }
           }
           slot = (slot + 1 == K) ? 0 : slot + 1;
@@ -1097,7 +1133,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
       tot = __longlong_as_double(0x7ff8000000000000ll);
       if (a.abort_word) atomicOr(a.abort_word, 1u);
     }
-    a.partials[int64_t(blockIdx.y) * gridDim.x + blockIdx.x] = tot;
+    const int64_t pi = int64_t(blockIdx.y) * gridDim.x + blockIdx.x;
+    if (LNCC_IN(pi, 1, a.n_parts)) a.partials[pi] = tot;
   }
 }
 

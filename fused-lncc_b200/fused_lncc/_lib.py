@@ -36,6 +36,7 @@ SIGNATURES = {
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
     "lncc_check_abort": (ctypes.c_int, [_vp, _vp]),
+    "lncc_checked_build": (ctypes.c_int, []),
     "lncc_wait_timeout_selftest": (ctypes.c_int, [_vp, ctypes.c_size_t, ctypes.c_uint, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),
     "lncc_set_companion": (ctypes.c_int, [ctypes.c_int]),

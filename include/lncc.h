@@ -42,7 +42,8 @@ enum lncc_status {
   LNCC_ERR_WORKSPACE = 6,       /* workspace missing or smaller than lncc_workspace_bytes() */
   LNCC_ERR_CUDA = 7,            /* other CUDA runtime error */
   LNCC_ERR_TOO_LARGE = 8,       /* size beyond a stated fixed maximum */
-  LNCC_ERR_ABORTED = 9          /* a bounded wait in the kernel timed out (lncc_check_abort) */
+  LNCC_ERR_ABORTED = 9,         /* a bounded wait in the kernel timed out (lncc_check_abort) */
+  LNCC_ERR_CHECK = 10           /* checked build only: a kernel index left its array */
 };
 
 /* Element types of pred / target / grad (the reference dispatches on the same two, lncc3d.cu:151-158). */
@@ -103,6 +104,16 @@ int lncc_fused_forward(const void* pred, const void* target, int dtype,
  * reference, whose kernels have no waits.
  */
 int lncc_check_abort(const void* workspace, cudaStream_t stream);
+
+/*
+ * 1 when this library is the bounds-checked build (compiled with LNCC_CHECKED=1, `build.py --checked`,
+ * file liblncc_sm100_checked.so), else 0. In the checked build every global, shared and tensor-memory
+ * access of the kernels is range-checked; an access outside its array is skipped and counted, and
+ * every entry point that launches kernels synchronises its stream and returns LNCC_ERR_CHECK when
+ * the count is not zero. It stands in for compute-sanitizer runs (the reference's
+ * tests/_sanitize2.py, tests/_sanitize_bf16.py). No counterpart in the reference.
+ */
+int lncc_checked_build(void);
 
 /*
  * Self-test of the bounded wait: one warp waits on an mbarrier that nothing completes, gives up after
