@@ -808,6 +808,7 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         }
       }
       const float2 nneg2 = make_float2(-nf, -nf);
+      const float2 ndr2 = make_float2(ndr, ndr);
       for (int it = 0; it < nsteps; ++it, ++s) {
         const int i = int(s & 1u);
         const uint32_t ph = (s >> 1) & 1u;
@@ -819,7 +820,8 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
         if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
         if (cvalid) {
           const float* dwp = &sm.dw[i][HR * h][0][px];
-          // running H sums: (Sp, St), (Spp, Stt) as f32x2 pairs, 2*Spt alone; windows of the last K rows
+          // running H sums: (Sp, St) and -n * (Spp, Stt) as f32x2 pairs, 2*Spt alone; windows of the
+          // last K rows
           float2 win01[K], win23[K];
           float win4[K];
           float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
@@ -837,11 +839,11 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
             const float v4 = lds((e * 5 + 4) * SPAN);
             if (e >= K) {
               s01 = add2(s01, sub2(v01, win01[e % K]));
-              s23 = add2(s23, sub2(v23, win23[e % K]));
+              s23 = fma2(nneg2, sub2(v23, win23[e % K]), s23);
               s4 += v4 - win4[e % K];
             } else {
               s01 = add2(s01, v01);
-              s23 = add2(s23, v23);
+              s23 = fma2(nneg2, v23, s23);
               s4 += v4;
             }
             win01[e % K] = v01;
@@ -851,9 +853,9 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
               const int k = e - 2 * R;  // stat row HR*h - R + k
               const float Sp = s01.x, St = s01.y;
               // (-VP', -VT') = (Sp^2 - n*Spp, St^2 - n*Stt); VP = max(n*Spp - Sp^2, 0) + n*dr, VT alike
-              const float2 mv = fma2(s01, s01, __fmul2_rn(nneg2, s23));
-              const float VP = ndr - fminf(mv.x, 0.f);
-              const float VT = ndr - fminf(mv.y, 0.f);
+              const float2 mv = fma2(s01, s01, s23);
+              const float2 vpt = sub2(ndr2, make_float2(fminf(mv.x, 0.f), fminf(mv.y, 0.f)));
+              const float VP = vpt.x, VT = vpt.y;
               const float Xc = fmaf(nh, s4, -(Sp * St));
               float rden;
               asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rden) : "f"(VP * VT));
