@@ -377,6 +377,62 @@ __global__ void __launch_bounds__(1024) lncc_reduce_kernel(const double* __restr
   }
 }
 
+// Loss of a batch sharded over ranks, one GPU each (lncc_peer_loss). Lane l (< world) writes this
+// rank's sum, then the epoch with system-scope release, into slot `rank` of rank l's exchange buffer
+// (peer memory over NVLink), then waits, bounded, until slot l of this rank's own buffer carries the
+// epoch and reads rank l's sum; the sums are added in rank order, so every rank gets the same bits.
+// Buffers: [2 epoch parities][world writers] x {double sum, uint64 epoch}; a rank one step ahead writes
+// the other parity, and two steps ahead it cannot be, since its next step needs this rank's sum.
+__global__ void __launch_bounds__(32) lncc_peer_loss_kernel(const double* __restrict__ local_sum,
+                                                          uint64_t* const* __restrict__ slots, int rank, int world,
+                                                          uint64_t epoch, double count, double* sum_out,
+                                                          float* loss_out, unsigned* abort_word,
+                                                          unsigned long long limit_ns) {
+  const int l = threadIdx.x;
+  const int par = int(epoch & 1u);
+  const double v = *local_sum;
+  if (l < world) {
+    uint64_t* dst = slots[l] + 2 * (par * world + rank);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(static_cast<uint64_t>(__double_as_longlong(v)))
+                 : "memory");
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst + 1), "l"(epoch) : "memory");
+  }
+  double got = 0.0;
+  bool ok = true;
+  if (l < world) {
+    const uint64_t* src = slots[rank] + 2 * (par * world + l);
+    unsigned long long t0 = 0, t = 0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+      uint64_t e;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(e) : "l"(src + 1) : "memory");
+      if (e == epoch) break;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > limit_ns) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (ok) {
+      uint64_t bits;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(bits) : "l"(src) : "memory");
+      got = __longlong_as_double(static_cast<long long>(bits));
+    }
+  }
+  double tot = 0.0;
+  for (int r = 0; r < world; ++r) tot += __shfl_sync(0xffffffffu, got, r);
+  const bool all_ok = __all_sync(0xffffffffu, ok);
+  if (l == 0) {
+    if (!all_ok) {
+      tot = __longlong_as_double(0x7ff8000000000000ll);
+      if (abort_word) atomicOr(abort_word, 1u);
+    }
+    if (sum_out) *sum_out = tot;
+    if (loss_out) *loss_out = float(1.0 - tot / count);
+  }
+}
+
 template <typename S>
 __global__ void lncc_scale_grad_kernel(S* __restrict__ g, int64_t n, const float* __restrict__ go) {
   const float s = __ldg(go);
@@ -1079,6 +1135,21 @@ int lncc_checked_build(void) {
 #else
   return 0;
 #endif
+}
+
+size_t lncc_peer_exchange_bytes(int world) {
+  if (world < 1 || world > 32) return 0;
+  return size_t(2) * size_t(world) * 2 * sizeof(uint64_t);
+}
+
+int lncc_peer_loss(const double* local_sum, void* const* slots, int rank, int world, uint64_t epoch, double count,
+                   double* cc_sum_out, float* loss_out, unsigned* abort_word, cudaStream_t stream) {
+  if (!local_sum || !slots || world < 1 || world > 32 || rank < 0 || rank >= world || epoch == 0 ||
+      !(count > 0.0) || (uintptr_t(slots) % 8))
+    return LNCC_ERR_BAD_ARG;
+  lncc_peer_loss_kernel<<<1, 32, 0, stream>>>(local_sum, reinterpret_cast<uint64_t* const*>(slots), rank, world,
+                                              epoch, count, cc_sum_out, loss_out, abort_word, ws::kWaitLimitNs);
+  return cudaGetLastError() == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 int lncc_check_abort(const void* workspace, cudaStream_t stream) {

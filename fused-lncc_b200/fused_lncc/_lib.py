@@ -36,6 +36,9 @@ SIGNATURES = {
     ]),
     "lncc_scale_grad": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _vp, _vp]),
     "lncc_check_abort": (ctypes.c_int, [_vp, _vp]),
+    "lncc_peer_exchange_bytes": (ctypes.c_size_t, [ctypes.c_int]),
+    "lncc_peer_loss": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_double,
+                                      _vp, _vp, _vp, _vp]),
     "lncc_checked_build": (ctypes.c_int, []),
     "lncc_wait_timeout_selftest": (ctypes.c_int, [_vp, ctypes.c_size_t, ctypes.c_uint, _vp]),
     "lncc_select_kernel": (ctypes.c_int, [ctypes.c_int]),

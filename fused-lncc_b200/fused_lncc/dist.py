@@ -5,14 +5,16 @@ Two partitions of the loss are provided here:
 
 * volume sharding (N*C volumes spread over ranks): the fused kernel runs unchanged on each rank's
   volumes. The gradient needs no collective because its scale, -1/M_global, is static. The loss needs
-  ONE all-reduce of one fp64 (the cc sum).
+  the sum of one fp64 per rank (the cc sum): on GPUs of one node through `PeerExchange`, one small
+  kernel that writes each rank's sum into every rank's buffer over NVLink peer memory and adds them in
+  rank order (no collective library on the step's path); otherwise one all-reduce.
 * D-slab sharding of single large volumes: see `slab_plan` / `SlabLNCC` (halo exchange of 2*(k//2)
   planes of pred and target with each neighbour, then the same fused kernel on the padded slab).
 """
 import torch
 import torch.distributed as dist
 
-from . import lncc_fused, scale_grad_
+from . import _lib, lncc_fused, scale_grad_
 
 
 def volume_range(n_volumes, world, rank):
@@ -30,6 +32,76 @@ def _world(group):
     return dist.get_world_size(group)
 
 
+class PeerExchange:
+    """Every rank's exchange buffer mapped into this process (CUDA IPC), for the C-ABI lncc_peer_loss.
+
+    Built once per (process group, device), collectively: each rank allocates its buffer, and the IPC
+    handles travel once through the group (all_gather_object). Afterwards a loss needs no collective:
+    `loss(local_sum, count)` launches one kernel on the current stream. The epoch counts calls and must
+    advance identically on every rank (every rank calls `loss` the same number of times).
+    """
+
+    def __init__(self, group=None, device=None):
+        from torch.multiprocessing.reductions import reduce_tensor
+        self.lib = _lib.load()
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = self.lib.lncc_peer_exchange_bytes(self.world)
+        if nbytes == 0:
+            raise RuntimeError(f"fused_lncc: peer exchange supports 1..32 ranks, not {self.world}")
+        self.buf = torch.zeros(nbytes // 8, dtype=torch.int64, device=self.device)
+        torch.cuda.synchronize(self.device)
+        shared = [None] * self.world
+        dist.all_gather_object(shared, reduce_tensor(self.buf), group=group)
+        self.peers = []
+        for r, (fn, args) in enumerate(shared):
+            if r == self.rank:
+                self.peers.append(self.buf)
+            else:
+                args = list(args)
+                args[6] = self.device.index  # open the peer's buffer from this process's device
+                self.peers.append(fn(*args))
+        self.slots = torch.tensor([t.data_ptr() for t in self.peers], dtype=torch.int64, device=self.device)
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def loss(self, local_sum, count, cc_sum_out=None):
+        """1 - (sum over ranks of local_sum) / count, on the current stream; every rank gets the same
+        bits. local_sum: 1-element fp64 device tensor. Returns a 0-dim fp32 tensor."""
+        self.epoch += 1
+        loss = torch.empty((), dtype=torch.float32, device=self.device)
+        st = self.lib.lncc_peer_loss(local_sum.data_ptr(), self.slots.data_ptr(), self.rank, self.world, self.epoch,
+                                     float(count), cc_sum_out.data_ptr() if cc_sum_out is not None else None,
+                                     loss.data_ptr(), None, torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "fused_lncc peer loss")
+        return loss
+
+
+_PEER = {}
+_PEER_ERR = {}  # why a group's exchange could not be built (diagnostics)
+
+
+def peer_exchange(group=None):
+    """The cached PeerExchange of `group` on the current device, or None when the group is not a
+    node-local NCCL group or the buffers cannot be mapped (the caller then all-reduces)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_backend(group) != "nccl":
+        return None
+    key = (id(group), torch.cuda.current_device())
+    if key not in _PEER:
+        px, err = None, None
+        try:
+            px = PeerExchange(group)
+        except Exception as e:  # e.g. ranks on several nodes: no peer mapping
+            err = e
+        # every rank must take the same path: use the exchange only where every rank built it
+        ok = torch.tensor([0 if px is None else 1], dtype=torch.int32, device=torch.cuda.current_device())
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        _PEER[key] = px if int(ok.item()) == 1 else None
+        _PEER_ERR[key] = err
+    return _PEER[key]
+
+
 class ShardedLNCC(torch.autograd.Function):
     """1 - (sum over all ranks of cc) / m_global, with dL/dpred_local (volume sharding)."""
 
@@ -38,11 +110,14 @@ class ShardedLNCC(torch.autograd.Function):
         cc_sum = torch.empty(1, dtype=torch.float64, device=pred.device)
         _, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=need_grad,
                           grad_scale=-1.0 / float(m_global), cc_sum_out=cc_sum)
-        if _world(group) > 1:
-            dist.all_reduce(cc_sum, op=dist.ReduceOp.SUM, group=group)
         ctx.save_for_backward(pred, target)
         ctx.args = (kernel_size, smooth_dr, m_global)
         ctx.grad = g
+        if _world(group) > 1:
+            px = peer_exchange(group)
+            if px is not None:
+                return px.loss(cc_sum, float(m_global))
+            dist.all_reduce(cc_sum, op=dist.ReduceOp.SUM, group=group)
         return (1.0 - cc_sum / float(m_global)).to(torch.float32).reshape(())
 
     @staticmethod

@@ -123,6 +123,27 @@ int lncc_checked_build(void);
 int lncc_wait_timeout_selftest(void* workspace, size_t workspace_bytes, unsigned limit_us, cudaStream_t stream);
 
 /*
+ * Loss of a batch whose volumes are sharded over `world` ranks of one node, one GPU each, without a
+ * collective library: a compute result followed by its reduction over NVLink peer memory in one
+ * small kernel. Each rank calls it on its own stream after lncc_fused_forward wrote its shard's
+ * sum of cc to local_sum (cc_sum_out). The kernel writes that sum into slot `rank` of every rank's
+ * exchange buffer, waits (bounded, 2 s) until every rank's sum of this epoch has arrived in its own
+ * buffer, and writes the same global sum (added in rank order, bitwise equal on every rank) and
+ * loss = 1 - sum / count on every rank.
+ *   slots : device array of `world` device pointers, slots[r] = rank r's exchange buffer mapped into
+ *           this process (CUDA IPC), lncc_peer_exchange_bytes(world) bytes each, zeroed once.
+ *   epoch : 1, 2, 3, ... one per call, the same on every rank.
+ *   abort_word: NULL or a device word set to 1 when another rank's sum did not arrive in time (the
+ *           sum and loss are then NaN).
+ * Replaces the fp64 all-reduce of the cc sum (no counterpart in the reference, which has no
+ * multi-GPU code).
+ */
+size_t lncc_peer_exchange_bytes(int world);
+int lncc_peer_loss(const double* local_sum, void* const* slots, int rank, int world, uint64_t epoch,
+                   double count, double* cc_sum_out, float* loss_out, unsigned* abort_word,
+                   cudaStream_t stream);
+
+/*
  * In place grad *= *grad_out for n elements of `dtype`; every block returns at once when
  * *grad_out == 1 (the usual loss.backward() case), so that case costs one tiny launch.
  * Replaces the `* (-grad_out / ctx.M)` tensor multiply of fused_lncc/__init__.py:73 (the -1/M part

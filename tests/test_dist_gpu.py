@@ -1,5 +1,6 @@
 """GPU, multi-process NCCL (needs >= 2 GPUs; skipped otherwise): the sharded losses equal the
-single-GPU loss of the whole batch / volume, and the gradients equal its slices."""
+single-GPU loss of the whole batch / volume, and the gradients equal its slices; the loss reduction
+over NVLink peer memory equals an NCCL all-reduce and gives every rank the same bits."""
 import datetime
 import os
 import socket
@@ -28,7 +29,25 @@ def _worker(rank, world, port, mode, q):
     try:
         from fused_lncc import fused_lncc_loss, synth
         from fused_lncc.dist import SlabPlan, sharded_lncc_loss, slab_lncc_loss, volume_range
-        if mode == "volumes":
+        if mode == "peer":
+            # the loss reduction over NVLink peer memory (lncc_peer_loss) against an NCCL all-reduce,
+            # over several epochs (both buffer parities), equal on every rank
+            from fused_lncc.dist import peer_exchange
+            px = peer_exchange()
+            assert px is not None, "peer exchange not available on this node"
+            worst = 0.0
+            for it in range(6):
+                local = torch.tensor([0.25 * (rank + 1) + it], dtype=torch.float64, device=dev)
+                s_out = torch.zeros(1, dtype=torch.float64, device=dev)
+                loss = px.loss(local, 10.0, cc_sum_out=s_out)
+                ref = local.clone()
+                dist.all_reduce(ref)
+                worst = max(worst, abs(s_out.item() - ref.item()), abs(loss.item() - (1.0 - ref.item() / 10.0)))
+                both = torch.stack([s_out[0], s_out[0]])
+                dist.broadcast(both, 0)  # rank 0's bits
+                worst = max(worst, abs(both[0].item() - s_out.item()))
+            q.put((rank, worst, 0.0))
+        elif mode == "volumes":
             p, t = synth.blurred_pair((2, 3, 40, 48, 64), device="cpu")
             p, t = p.to(dev), t.to(dev)
             pf = p.clone().requires_grad_(True)
@@ -66,7 +85,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["volumes", "slabs"])
+@pytest.mark.parametrize("mode", ["volumes", "slabs", "peer"])
 def test_two_gpu_sharding_matches_single_gpu(mode):
     world = 2
     ctx = mp.get_context("spawn")
