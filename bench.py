@@ -484,6 +484,9 @@ def main():
         kname = "lncc_ws_kernel" if W % 4 == 0 else "lncc_sweep_kernel"
         launches_per_call = max(1, lib.lncc_launch_count(nb, D, H, W, k, dtc, z_rng[0], z_rng[1], 1))
         traffic = profile_traffic(kname, args.workload) if world == 1 else None
+        # the loss of a sharded step: one peer-memory reduction kernel of ours (else NCCL's all-reduce)
+        from fused_lncc import dist as fdist
+        peer_kernels = 1 if world > 1 and any(v is not None for v in fdist._PEER.values()) else 0
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
             "steps": args.steps,
@@ -505,8 +508,9 @@ def main():
                     "ms_per_step": ms_e2e},
             # per compute call the fused kernel (plus its companion launch on idle SMs when the
             # library plans one) and the loss reduction, 3 calls per slab step when halos are
-            # exchanged (to overlap the interior); plus the grad_out scale kernel
-            "gpu_launches": ((launches_per_call + 1) * (3 if slabs and world > 1 else 1) + 1) * args.steps,
+            # exchanged (to overlap the interior); plus the grad_out scale kernel and, at N > 1, the
+            # peer-memory loss kernel
+            "gpu_launches": ((launches_per_call + 1) * (3 if slabs and world > 1 else 1) + 1 + peer_kernels) * args.steps,
             "clocks": clocks,
             "loss": loss_val,
         }

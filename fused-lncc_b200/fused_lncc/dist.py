@@ -253,9 +253,12 @@ class SlabLNCC(torch.autograd.Function):
         for z0, z1 in ((lo, i0), (max(i1, i0), e)):
             if z1 > z0:
                 total += compute(pred_slab, target_slab, kernel_size, smooth_dr, (z0, z1), gscale, g)
-        if _world(group) > 1:
-            dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
         ctx.grad = g
+        if _world(group) > 1:
+            px = peer_exchange(group) if total.is_cuda else None
+            if px is not None:
+                return px.loss(total, float(m_global))
+            dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
         return (1.0 - total / float(m_global)).to(torch.float32).reshape(())
 
     @staticmethod
