@@ -439,6 +439,59 @@ def test_ws_companion_under_graph_capture():
     del graph
 
 
+def test_ws_companion_two_host_threads():
+    """Two host threads, each on a stream of its own, call the companion path concurrently and each
+    captures and replays a graph of it: the library's second stream and events are per (thread,
+    device), so neither thread's fork or join orders the other's work, and every result equals the
+    single-threaded one bit for bit."""
+    import threading
+    from fused_lncc import synth
+    shapes = [(1, 8, 64, 128, 128), (1, 1, 512, 128, 128)]
+    inputs = [synth.blurred_pair(sh, device="cuda") for sh in shapes]
+    ref = []
+    for p, t in inputs:
+        s = torch.zeros((), dtype=torch.float64, device="cuda")
+        _, g = lncc_fused(p, t, 7, cc_sum_out=s)
+        ref.append((s.clone(), g.clone()))
+    torch.cuda.synchronize()
+    errors = []
+
+    def work(idx):
+        try:
+            p, t = inputs[idx]
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                s = torch.zeros((), dtype=torch.float64, device="cuda")
+                g = torch.empty_like(p)
+                for _ in range(6):
+                    s.zero_()
+                    lncc_fused(p, t, 7, cc_sum_out=s, out=g)
+                    if not (torch.equal(s, ref[idx][0]) and torch.equal(g, ref[idx][1])):
+                        errors.append((idx, "eager"))
+                stream.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+                    lncc_fused(p, t, 7, cc_sum_out=s, out=g)
+                for _ in range(4):
+                    s.zero_()
+                    g.zero_()
+                    graph.replay()
+                    if not (torch.equal(s, ref[idx][0]) and torch.equal(g, ref[idx][1])):
+                        errors.append((idx, "replay"))
+                stream.synchronize()
+                del graph
+        except Exception as e:  # noqa: BLE001 - reported by the main thread
+            errors.append((idx, repr(e)))
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(2)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    assert not any(th.is_alive() for th in threads)
+    assert not errors, errors
+
+
 def test_bf16_k9_and_loss_only():
     from fused_lncc import synth
     pred, target = synth.blurred_pair((2, 2, 40, 64, 64), device="cuda", dtype=torch.bfloat16)
