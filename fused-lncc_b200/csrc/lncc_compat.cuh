@@ -44,6 +44,10 @@ struct Args {
   int D, H, W;
   int tiles_x, tiles_y, chunks;
   float n, ndr, scale;
+  const float* scale_dev;  // BWD: null, or a device float that also multiplies the gradient
+  double* partials;    // MAPS: null, or one fp64 sum of the clamped cc per block (the loss)
+  int64_t n_parts;     // entries writable at partials
+  int rd, rh, rw;      // ANISO: window half-widths along D, H, W (0 .. R each)
 };
 
 template <typename S> __device__ __forceinline__ float ld(const S* p);
@@ -56,16 +60,24 @@ template <> __device__ __forceinline__ void st<float>(float* p, float v) { *p = 
 template <> __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, float v) {
   *p = __float2bfloat16_rn(v);
 }
+template <> __device__ __forceinline__ float ld<__half>(const __half* p) { return __half2float(__ldg(p)); }
+template <> __device__ __forceinline__ void st<__half>(__half* p, float v) { *p = __float2half_rn(v); }
 
 // S: element type of pred/target (MAPS inputs, BWD output); the maps and box3d data are fp32.
-template <int R, int MODE, typename S>
+// ANISO = false: the cubic window k = 2R + 1. ANISO = true: a kd x kh x kw window with the half-widths
+// a.rd, a.rh, a.rw (each at most R, which sizes the shared arrays); n = kd * kh * kw comes in a.n.
+template <int R, int MODE, typename S, bool ANISO = false>
 __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
   constexpr int NF = Fields<MODE>::NF;
-  constexpr int K = 2 * R + 1;
-  constexpr int FH = TH + 2 * R, FW = TW + 2 * R, FP = FH * FW;
-  constexpr int PPT = (FP + NT - 1) / NT;
-  __shared__ float DS[NF][FH][FW];  // D-window sums of the current output plane, footprint
-  __shared__ float HS[NF][TH][FW];  // after the H box
+  constexpr int FHM = TH + 2 * R, FWM = TW + 2 * R, FPM = FHM * FWM;  // largest footprint
+  constexpr int PPT = (FPM + NT - 1) / NT;
+  __shared__ float DS[NF][FHM][FWM];  // D-window sums of the current output plane, footprint
+  __shared__ float HS[NF][TH][FWM];   // after the H box
+  __shared__ double red[NT / 32];
+  // compile-time constants in the cubic instantiations
+  const int rd = ANISO ? a.rd : R, rh = ANISO ? a.rh : R, rw = ANISO ? a.rw : R;
+  const int kh = 2 * rh + 1, kw = 2 * rw + 1;
+  const int FH = TH + 2 * rh, FW = TW + 2 * rw, FP = FH * FW;
 
   const int tid = threadIdx.x;
   int64_t bid = blockIdx.x;
@@ -83,7 +95,7 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
 #pragma unroll
   for (int j = 0; j < PPT; ++j) {
     const int i = tid + j * NT;
-    const int gy = y0 - R + i / FW, gx = x0 - R + i % FW;
+    const int gy = y0 - rh + i / FW, gx = x0 - rw + i % FW;
     in[j] = i < FP && gy >= 0 && gy < a.H && gx >= 0 && gx < a.W;
     off[j] = in[j] ? int64_t(gy) * a.W + gx : 0;
   }
@@ -113,14 +125,15 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
     }
   };
 
-  for (int z = z0 - R; z < z0 + R; ++z) accum(z, 1.f);
+  double cc_acc = 0.0;  // MAPS with partials: this thread's sum of the clamped cc
+  for (int z = z0 - rd; z < z0 + rd; ++z) accum(z, 1.f);
   for (int z = z0; z < z1; ++z) {
-    accum(z + R, 1.f);
-    if (z > z0) accum(z - R - 1, -1.f);
+    accum(z + rd, 1.f);
+    if (z > z0) accum(z - rd - 1, -1.f);
 #pragma unroll
     for (int j = 0; j < PPT; ++j) {
       const int i = tid + j * NT;
-      if (i < FP && LNCC_IN(i, 1, FH * FW)) {
+      if (i < FP && LNCC_IN((i / FW) * FWM + i % FW, 1, FHM * FWM)) {
 #pragma unroll
         for (int f = 0; f < NF; ++f) DS[f][i / FW][i % FW] = s[j][f];
       }
@@ -132,8 +145,8 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
       for (int f = 0; f < NF; ++f) {
         float h = 0.f;
 #pragma unroll
-        for (int d = 0; d < K; ++d) h += DS[f][r + d][c];
-        if (LNCC_IN((r + K - 1) * FW + c, 1, FH * FW) && LNCC_IN(r * FW + c, 1, TH * FW)) HS[f][r][c] = h;
+        for (int d = 0; d < kh; ++d) h += DS[f][r + d][c];
+        if (LNCC_IN((r + kh - 1) * FWM + c, 1, FHM * FWM) && LNCC_IN(r * FWM + c, 1, TH * FWM)) HS[f][r][c] = h;
       }
     }
     __syncthreads();
@@ -146,11 +159,11 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
       for (int f = 0; f < NF; ++f) {
         float h = 0.f;
 #pragma unroll
-        for (int d = 0; d < K; ++d) h += HS[f][r][c + d];
+        for (int d = 0; d < kw; ++d) h += HS[f][r][c + d];
         w[f] = h;
       }
       const int64_t o = vol + int64_t(z) * HW + int64_t(y) * a.W + x;
-      if (!LNCC_IN(o, 1, a.n_elems) || !LNCC_IN(r * FW + c + K - 1, 1, TH * FW)) continue;
+      if (!LNCC_IN(o, 1, a.n_elems) || !LNCC_IN(r * FWM + c + kw - 1, 1, TH * FWM)) continue;
       if (MODE == MAPS) {
         // n-scaled statistics (X = n*cross, VP = n*var_p, VT = n*var_t): the same cancellation of
         // constant inputs as the reference's division by n, and the same maps:
@@ -176,18 +189,31 @@ __global__ void __launch_bounds__(NT) compat_kernel(const Args a) {
           Bc *= gw;
           Cc *= gw;
         }
+        cc_acc += double(cc);
         if (a.out[0]) static_cast<float*>(a.out[0])[o] = a.loss_map ? 1.f - cc : cc;
         if (a.out[1]) static_cast<float*>(a.out[1])[o] = A;
         if (a.out[2]) static_cast<float*>(a.out[2])[o] = Bc;
         if (a.out[3]) static_cast<float*>(a.out[3])[o] = Cc;
       } else if (MODE == BWD) {
         const float p = ld(static_cast<const S*>(a.p) + o), t = ld(static_cast<const S*>(a.t) + o);
-        st(static_cast<S*>(a.out[0]) + o, a.scale * (w[0] + 2.f * p * w[1] + t * w[2]));
+        const float sc = a.scale_dev ? a.scale * __ldg(a.scale_dev) : a.scale;
+        st(static_cast<S*>(a.out[0]) + o, sc * (w[0] + 2.f * p * w[1] + t * w[2]));
       } else {
         static_cast<float*>(a.out[0])[o] = w[0];
       }
     }
     // the next plane's DS writes follow this thread's W pass; its H pass follows the next barrier
+  }
+  if (MODE == MAPS && a.partials) {  // block sum of the clamped cc, in a fixed order
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cc_acc += __shfl_down_sync(0xffffffffu, cc_acc, o);
+    if ((tid & 31) == 0) red[tid >> 5] = cc_acc;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < NT / 32; ++w) t += red[w];
+      if (LNCC_IN(blockIdx.x, 1, a.n_parts)) a.partials[blockIdx.x] = t;
+    }
   }
 }
 

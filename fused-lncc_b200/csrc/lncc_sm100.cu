@@ -28,6 +28,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <atomic>
@@ -53,6 +54,11 @@ template <> __device__ __forceinline__ void stg<float>(float* p, float v) { *p =
 template <> __device__ __forceinline__ void stg<__nv_bfloat16>(__nv_bfloat16* p, float v) {
   *p = __float2bfloat16_rn(v);
 }
+template <> __device__ __forceinline__ float ldf<__half>(const __half* p) { return __half2float(__ldg(p)); }
+__device__ __forceinline__ float tof(float v) { return v; }
+__device__ __forceinline__ float tof(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float tof(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ void stg<__half>(__half* p, float v) { *p = __float2half_rn(v); }
 
 // ------------------------------------------------------------------------------------------------
 // geometry of the sweep kernel (all in fp32 words of shared memory)
@@ -439,10 +445,7 @@ __global__ void lncc_scale_grad_kernel(S* __restrict__ g, int64_t n, const float
   if (s == 1.f) return;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x) {
-    float v;
-    if constexpr (sizeof(S) == 4) v = g[i];
-    else v = __bfloat162float(g[i]);
-    stg<S>(g + i, v * s);
+    stg<S>(g + i, tof(g[i]) * s);  // a plain load: g is written by this kernel
   }
 }
 
@@ -535,6 +538,16 @@ static size_t smem_needed(int R) {
 }
 
 static bool valid_k(int k) { return k == 3 || k == 5 || k == 7 || k == 9; }
+static bool valid_dtype(int dtype) { return dtype == LNCC_F32 || dtype == LNCC_BF16 || dtype == LNCC_F16; }
+static size_t dtype_size(int dtype) { return dtype == LNCC_F32 ? 4 : 2; }
+// Calls f with a value of the element type of `dtype` (float, __nv_bfloat16 or __half); the caller
+// has checked valid_dtype.
+template <typename F>
+static auto with_dtype(int dtype, F&& f) {
+  if (dtype == LNCC_F32) return f(float{});
+  if (dtype == LNCC_BF16) return f(__nv_bfloat16{});
+  return f(__half{});
+}
 
 // Workspace layout: a 16-byte header whose first word records a timed-out wait of the last call
 // (lncc_check_abort), then the fp64 loss partials.
@@ -558,7 +571,7 @@ constexpr int kWsMaxTall = 16;     // non-portable cluster size, tried for plane
 // accesses) when W % 8 == 0 and the base pointers are aligned to a chunk, else 4 columns when
 // W % 4 == 0 and aligned to that; 0 = the kernel does not apply.
 static int ws_chunk(int64_t W, int dtype, const void* p, const void* t, const void* g) {
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   auto aligned = [&](uintptr_t al) {
     return !((uintptr_t(p) % al) || (uintptr_t(t) % al) || (g && (uintptr_t(g) % al)));
   };
@@ -614,10 +627,10 @@ static cudaError_t ws_fn_cw(int R, int cw, bool assist, const void** fn) {
 }
 
 static cudaError_t ws_kernel_fn(int R, int dtype, bool grad, int cw, bool assist, const void** fn) {
-  if (dtype == LNCC_F32)
-    return grad ? ws_fn_cw<float, true>(R, cw, assist, fn) : ws_fn_cw<float, false>(R, cw, assist, fn);
-  return grad ? ws_fn_cw<__nv_bfloat16, true>(R, cw, assist, fn)
-              : ws_fn_cw<__nv_bfloat16, false>(R, cw, assist, fn);
+  return with_dtype(dtype, [&](auto tag) {
+    using S = decltype(tag);
+    return grad ? ws_fn_cw<S, true>(R, cw, assist, fn) : ws_fn_cw<S, false>(R, cw, assist, fn);
+  });
 }
 
 static int ws_smem_for(int R) {
@@ -851,7 +864,7 @@ static cudaError_t launch_ws(const WsPlan& wp, const ws::Args& wa, cudaStream_t 
     return launch_ws_grid(wp, wp.cy, nc, a1, st);
   }
   *nparts = wp.parts();
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   ws::Args a1 = wa, a2 = wa;
   if (wp.z2 > 0) {  // every volume: the main launch takes planes [z_begin, zs), the companion [zs, z_end)
     const int zs = wa.z_end - int(wp.z2);
@@ -930,6 +943,36 @@ static cudaError_t launch_compat(int R, const compat::Args& a, int64_t nblocks, 
   return cudaGetLastError();
 }
 
+// Window of the materialising paths: cubic (k = kd = kh = kw in {3,5,7,9}, the compiled radii) or any
+// kd x kh x kw with each side odd in 1 .. 9 (one instantiation of radius 4, the radii at run time).
+struct Win {
+  int kd, kh, kw;
+  bool cubic() const { return kd == kh && kh == kw && valid_k(kd); }
+};
+static bool valid_side(int k) { return k >= 1 && k <= 9 && (k & 1); }
+constexpr int kAnisoMaxR = 4;
+
+template <int MODE, typename S>
+static cudaError_t launch_compat_w(const Win& w, const compat::Args& a, int64_t nblocks, cudaStream_t st) {
+  if (w.cubic()) return launch_compat<MODE, S>(w.kd / 2, a, nblocks, st);
+  compat::compat_kernel<kAnisoMaxR, MODE, S, true><<<dim3(unsigned(nblocks)), dim3(compat::NT), 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+static int compat_plan(int64_t B, int64_t D, int64_t H, int64_t W, int k, compat::Args* a, int64_t* nblocks);
+// As compat_plan, for a window of any odd sides in 1 .. 9 (sets the radii and n = kd*kh*kw).
+static int compat_plan_w(int64_t B, int64_t D, int64_t H, int64_t W, const Win& w, compat::Args* a,
+                         int64_t* nblocks) {
+  if (!valid_side(w.kd) || !valid_side(w.kh) || !valid_side(w.kw)) return LNCC_ERR_KERNEL_SIZE;
+  const int st = compat_plan(B, D, H, W, w.cubic() ? w.kd : 3, a, nblocks);
+  if (st != LNCC_OK) return st;
+  a->rd = w.kd / 2;
+  a->rh = w.kh / 2;
+  a->rw = w.kw / 2;
+  a->n = float(w.kd * w.kh * w.kw);
+  return LNCC_OK;
+}
+
 // Geometry and size checks shared by the three compat entry points; fills the tiling fields of `a`.
 static int compat_plan(int64_t B, int64_t D, int64_t H, int64_t W, int k, compat::Args* a, int64_t* nblocks) {
   if (!valid_k(k)) return LNCC_ERR_KERNEL_SIZE;
@@ -982,7 +1025,7 @@ const char* lncc_strerror(int status) {
     case LNCC_OK: return "ok";
     case LNCC_ERR_BAD_ARG: return "fused_lncc: bad argument (null pointer, size or plane range)";
     case LNCC_ERR_KERNEL_SIZE: return "fused_lncc: kernel_size not supported (odd 3..9)";
-    case LNCC_ERR_DTYPE: return "fused_lncc: float32 or bfloat16 only";
+    case LNCC_ERR_DTYPE: return "fused_lncc: float32, bfloat16 or float16 only";
     case LNCC_ERR_LAUNCH: return "fused_lncc: kernel launch failed";
     case LNCC_ERR_SMEM: return "fused_lncc: shared memory need exceeds this GPU's opt-in cap";
     case LNCC_ERR_WORKSPACE: return "fused_lncc: workspace missing or too small";
@@ -1000,7 +1043,7 @@ size_t lncc_workspace_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int kern
                             int64_t z_begin, int64_t z_end) {
   if (B < 1 || D < 1 || H < 1 || W < 1 || !valid_k(kernel_size)) return 0;
   if (z_begin < 0 || z_end > D || z_end <= z_begin) return 0;
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return 0;
+  if (!valid_dtype(dtype)) return 0;
   // enough for either kernel (the choice also depends on pointer alignment, known only at launch)
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
   size_t need = size_t(pl.nblocks) * sizeof(double);
@@ -1017,12 +1060,12 @@ static int impl_lncc_fused_forward(const void* pred, const void* target, int dty
                        float* loss_out, double loss_count, void* workspace, size_t workspace_bytes,
                        cudaStream_t stream) {
   if (!valid_k(kernel_size)) return LNCC_ERR_KERNEL_SIZE;
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   if (!pred || !target) return LNCC_ERR_BAD_ARG;
   if (B < 1 || D < 1 || H < 1 || W < 1) return LNCC_ERR_BAD_ARG;
   if (z_begin < 0 || z_end > D || z_end <= z_begin) return LNCC_ERR_BAD_ARG;
   if (D > INT32_MAX / 2 || H * W > INT32_MAX) return LNCC_ERR_TOO_LARGE;
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (grad && uintptr_t(grad) % esz))
     return LNCC_ERR_BAD_ARG;
   const Plan pl = make_plan(B, H, W, kernel_size, z_begin, z_end);
@@ -1091,12 +1134,12 @@ static int impl_lncc_fused_forward(const void* pred, const void* target, int dty
     wa.total_items = wp.total;
     wa.items_per_cluster = wp.ipc;
     e = launch_ws(wp, wa, stream, B, D, H, W, dtype, &nparts);
-  } else if (dtype == LNCC_F32)
-    e = g ? dispatch_r<float, true>(pl.R, a, pl.nblocks, stream)
-          : dispatch_r<float, false>(pl.R, a, pl.nblocks, stream);
-  else
-    e = g ? dispatch_r<__nv_bfloat16, true>(pl.R, a, pl.nblocks, stream)
-          : dispatch_r<__nv_bfloat16, false>(pl.R, a, pl.nblocks, stream);
+  } else {
+    e = with_dtype(dtype, [&](auto tag) {
+      using S = decltype(tag);
+      return g ? dispatch_r<S, true>(pl.R, a, pl.nblocks, stream) : dispatch_r<S, false>(pl.R, a, pl.nblocks, stream);
+    });
+  }
   if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
   if (cc_sum_out || loss_out) {
     lncc_reduce_kernel<<<1, 1024, 0, stream>>>(a.partials, int(nparts), cc_sum_out, loss_out,
@@ -1181,7 +1224,7 @@ int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_siz
                       int64_t z_end, int grad) {
   // errors are negative so that they never read as a count
   if (!valid_k(kernel_size)) return -LNCC_ERR_KERNEL_SIZE;
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return -LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return -LNCC_ERR_DTYPE;
   if (B < 1 || D < 1 || H < 1 || W < 1 || z_begin < 0 || z_end > D || z_end <= z_begin) return -LNCC_ERR_BAD_ARG;
   const WsPlan wp = make_ws_plan(B, H, W, kernel_size, dtype, grad != 0, z_begin, z_end, nullptr, nullptr, nullptr);
   return (wp.ok && (wp.b2 > 0 || wp.z2 > 0)) ? 2 : 1;
@@ -1190,13 +1233,13 @@ int lncc_launch_count(int64_t B, int64_t D, int64_t H, int64_t W, int kernel_siz
 static int impl_lncc_maps_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                       int64_t W, int kernel_size, float smooth_dr, float* ncc, float* A, float* Bc, float* Cc,
                       cudaStream_t stream) {
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   compat::Args a = {};
   int64_t nb = 0;
   const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
   if (st != LNCC_OK) return st;
   if (!pred || !target) return LNCC_ERR_BAD_ARG;
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz)) return LNCC_ERR_BAD_ARG;
   for (const float* m : {static_cast<const float*>(ncc), static_cast<const float*>(A),
                          static_cast<const float*>(Bc), static_cast<const float*>(Cc)})
@@ -1208,21 +1251,20 @@ static int impl_lncc_maps_forward(const void* pred, const void* target, int dtyp
   a.out[2] = Bc;
   a.out[3] = Cc;
   a.ndr = a.n * smooth_dr;
-  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
-                                          : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  const cudaError_t e = with_dtype(dtype, [&](auto tag) { return launch_compat<compat::MAPS, decltype(tag)>(kernel_size / 2, a, nb, stream); });
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 static int impl_lncc_maps_backward(const float* A, const float* Bc, const float* Cc, const void* pred, const void* target,
                        int dtype, int64_t B, int64_t D, int64_t H, int64_t W, int kernel_size, float scale,
                        void* grad, cudaStream_t stream) {
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   compat::Args a = {};
   int64_t nb = 0;
   const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
   if (st != LNCC_OK) return st;
   if (!A || !Bc || !Cc || !pred || !target || !grad) return LNCC_ERR_BAD_ARG;
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(grad) % esz)) return LNCC_ERR_BAD_ARG;
   if ((uintptr_t(A) % 4) || (uintptr_t(Bc) % 4) || (uintptr_t(Cc) % 4)) return LNCC_ERR_BAD_ARG;
   a.in[0] = A;
@@ -1232,8 +1274,7 @@ static int impl_lncc_maps_backward(const float* A, const float* Bc, const float*
   a.t = target;
   a.out[0] = grad;
   a.scale = scale;
-  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::BWD, float>(kernel_size / 2, a, nb, stream)
-                                          : launch_compat<compat::BWD, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  const cudaError_t e = with_dtype(dtype, [&](auto tag) { return launch_compat<compat::BWD, decltype(tag)>(kernel_size / 2, a, nb, stream); });
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
@@ -1256,35 +1297,34 @@ size_t lncc_loss_map_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W) {
 }
 
 static int impl_lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
-                          int64_t W, int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream) {
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+                          int64_t W, const Win& win, float smooth_dr, float* loss_map, cudaStream_t stream) {
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   compat::Args a = {};
   int64_t nb = 0;
-  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  const int st = compat_plan_w(B, D, H, W, win, &a, &nb);
   if (st != LNCC_OK) return st;
   if (!pred || !target || !loss_map) return LNCC_ERR_BAD_ARG;
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(loss_map) % 4)) return LNCC_ERR_BAD_ARG;
   a.in[0] = pred;
   a.in[1] = target;
   a.out[0] = loss_map;
   a.loss_map = 1;
   a.ndr = a.n * smooth_dr;
-  const cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
-                                          : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  const cudaError_t e = with_dtype(dtype, [&](auto tag) { return launch_compat_w<compat::MAPS, decltype(tag)>(win, a, nb, stream); });
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 static int impl_lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
-                           int64_t D, int64_t H, int64_t W, int kernel_size, float smooth_dr, void* grad,
+                           int64_t D, int64_t H, int64_t W, const Win& win, float smooth_dr, void* grad,
                            float* scratch, size_t scratch_bytes, cudaStream_t stream) {
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   compat::Args a = {};
   int64_t nb = 0;
-  const int st = compat_plan(B, D, H, W, kernel_size, &a, &nb);
+  const int st = compat_plan_w(B, D, H, W, win, &a, &nb);
   if (st != LNCC_OK) return st;
   if (!grad_map || !pred || !target || !grad) return LNCC_ERR_BAD_ARG;
-  const size_t esz = dtype == LNCC_F32 ? 4 : 2;
+  const size_t esz = dtype_size(dtype);
   if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (uintptr_t(grad) % esz) ||
       (uintptr_t(grad_map) % 4))
     return LNCC_ERR_BAD_ARG;
@@ -1302,8 +1342,7 @@ static int impl_lncc_loss_map_backward(const float* grad_map, const void* pred, 
   a.out[3] = mC;
   a.wmap = grad_map;
   a.ndr = a.n * smooth_dr;
-  cudaError_t e = dtype == LNCC_F32 ? launch_compat<compat::MAPS, float>(kernel_size / 2, a, nb, stream)
-                                    : launch_compat<compat::MAPS, __nv_bfloat16>(kernel_size / 2, a, nb, stream);
+  cudaError_t e = with_dtype(dtype, [&](auto tag) { return launch_compat_w<compat::MAPS, decltype(tag)>(win, a, nb, stream); });
   if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
   compat::Args b = a;
   b.in[0] = mA;
@@ -1315,25 +1354,88 @@ static int impl_lncc_loss_map_backward(const float* grad_map, const void* pred, 
   b.out[1] = b.out[2] = b.out[3] = nullptr;
   b.wmap = nullptr;
   b.scale = -1.f;
-  e = dtype == LNCC_F32 ? launch_compat<compat::BWD, float>(kernel_size / 2, b, nb, stream)
-                        : launch_compat<compat::BWD, __nv_bfloat16>(kernel_size / 2, b, nb, stream);
+  e = with_dtype(dtype, [&](auto tag) { return launch_compat_w<compat::BWD, decltype(tag)>(win, b, nb, stream); });
+  return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
+}
+
+// Non-cubic window: adjoint maps (A, Bc, Cc, fp32, in the scratch) and the per-block cc sums in one
+// pass, the loss from those sums, then the maps backward for the gradient.
+static size_t aniso_parts(int64_t B, int64_t D, int64_t H, int64_t W) {
+  compat::Args a = {};
+  int64_t nb = 0;
+  return compat_plan(B, D, H, W, 3, &a, &nb) == LNCC_OK ? size_t(nb) : 0;
+}
+
+size_t lncc_aniso_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int with_grad) {
+  const size_t nb = aniso_parts(B, D, H, W);
+  if (nb == 0) return 0;
+  const size_t maps = with_grad ? size_t(3) * size_t(B) * size_t(D) * size_t(H) * size_t(W) * sizeof(float) : 0;
+  return nb * sizeof(double) + maps;
+}
+
+static int impl_lncc_aniso_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                                   int64_t W, const Win& win, float smooth_dr, void* grad, float grad_scale,
+                                   const float* grad_scale_dev, double* cc_sum_out, float* loss_out,
+                                   double loss_count, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
+  compat::Args a = {};
+  int64_t nb = 0;
+  const int st = compat_plan_w(B, D, H, W, win, &a, &nb);
+  if (st != LNCC_OK) return st;
+  if (!pred || !target) return LNCC_ERR_BAD_ARG;
+  const size_t esz = dtype_size(dtype);
+  if ((uintptr_t(pred) % esz) || (uintptr_t(target) % esz) || (grad && uintptr_t(grad) % esz)) return LNCC_ERR_BAD_ARG;
+  const size_t need = lncc_aniso_scratch_bytes(B, D, H, W, grad != nullptr);
+  if (!scratch || scratch_bytes < need || (uintptr_t(scratch) % 8)) return LNCC_ERR_WORKSPACE;
+  double* parts = static_cast<double*>(scratch);
+  const size_t nvox = size_t(B) * size_t(D) * size_t(H) * size_t(W);
+  float* maps = reinterpret_cast<float*>(parts + nb);
+  a.in[0] = pred;
+  a.in[1] = target;
+  if (grad) {
+    a.out[1] = maps;
+    a.out[2] = maps + nvox;
+    a.out[3] = maps + 2 * nvox;
+  }
+  a.partials = parts;
+  a.n_parts = nb;
+  a.ndr = a.n * smooth_dr;
+  cudaError_t e = with_dtype(dtype, [&](auto tag) { return launch_compat_w<compat::MAPS, decltype(tag)>(win, a, nb, stream); });
+  if (e != cudaSuccess) return LNCC_ERR_LAUNCH;
+  if (cc_sum_out || loss_out) {
+    lncc_reduce_kernel<<<1, 1024, 0, stream>>>(parts, int(nb), cc_sum_out, loss_out,
+                                               loss_count > 0.0 ? loss_count : double(nvox));
+    if (cudaGetLastError() != cudaSuccess) return LNCC_ERR_LAUNCH;
+  }
+  if (!grad) return LNCC_OK;
+  compat::Args b = a;
+  b.in[0] = a.out[1];
+  b.in[1] = a.out[2];
+  b.in[2] = a.out[3];
+  b.p = pred;
+  b.t = target;
+  b.out[0] = grad;
+  b.out[1] = b.out[2] = b.out[3] = nullptr;
+  b.partials = nullptr;
+  b.scale = grad_scale;
+  b.scale_dev = grad_scale_dev;
+  e = with_dtype(dtype, [&](auto tag) { return launch_compat_w<compat::BWD, decltype(tag)>(win, b, nb, stream); });
   return e == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
 static int impl_lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {
-  if (dtype != LNCC_F32 && dtype != LNCC_BF16) return LNCC_ERR_DTYPE;
+  if (!valid_dtype(dtype)) return LNCC_ERR_DTYPE;
   if (!grad || !grad_out_dev || n < 0) return LNCC_ERR_BAD_ARG;
   if (n == 0) return LNCC_OK;
   const int threads = 256;
   int64_t blocks = (n + threads - 1) / threads;
   const int64_t cap = 8LL * sm_count_current();
   if (blocks > cap) blocks = cap;
-  if (dtype == LNCC_F32)
-    lncc_scale_grad_kernel<float><<<unsigned(blocks), threads, 0, stream>>>(
-        reinterpret_cast<float*>(grad), n, grad_out_dev);
-  else
-    lncc_scale_grad_kernel<__nv_bfloat16><<<unsigned(blocks), threads, 0, stream>>>(
-        reinterpret_cast<__nv_bfloat16*>(grad), n, grad_out_dev);
+  with_dtype(dtype, [&](auto tag) {
+    using S = decltype(tag);
+    lncc_scale_grad_kernel<S><<<unsigned(blocks), threads, 0, stream>>>(static_cast<S*>(grad), n, grad_out_dev);
+    return 0;
+  });
   return cudaGetLastError() == cudaSuccess ? LNCC_OK : LNCC_ERR_LAUNCH;
 }
 
@@ -1385,28 +1487,53 @@ int lncc_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_
 #endif
 }
 
+#ifdef LNCC_CHECKED
+#define LNCC_ENTRY(body, stream) LNCC_CHECKED_ENTRY(body, stream)
+#else
+#define LNCC_ENTRY(body, stream) return (body)
+#endif
+
 int lncc_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
                           int64_t W, int kernel_size, float smooth_dr, float* loss_map, cudaStream_t stream) {
-#ifdef LNCC_CHECKED
-  LNCC_CHECKED_ENTRY(impl_lncc_loss_map_forward(
-      pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, loss_map, stream), stream);
-#else
-  return impl_lncc_loss_map_forward(pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, loss_map, stream);
-#endif
+  if (!valid_k(kernel_size)) return LNCC_ERR_KERNEL_SIZE;
+  const Win win{kernel_size, kernel_size, kernel_size};
+  LNCC_ENTRY(impl_lncc_loss_map_forward(pred, target, dtype, B, D, H, W, win, smooth_dr, loss_map, stream), stream);
 }
 
 int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
                            int64_t D, int64_t H, int64_t W, int kernel_size, float smooth_dr, void* grad,
                            float* scratch, size_t scratch_bytes, cudaStream_t stream) {
-#ifdef LNCC_CHECKED
-  LNCC_CHECKED_ENTRY(impl_lncc_loss_map_backward(
-      grad_map, pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, grad, scratch, scratch_bytes,
-      stream), stream);
-#else
-  return impl_lncc_loss_map_backward(
-      grad_map, pred, target, dtype, B, D, H, W, kernel_size, smooth_dr, grad, scratch, scratch_bytes,
-      stream);
-#endif
+  if (!valid_k(kernel_size)) return LNCC_ERR_KERNEL_SIZE;
+  const Win win{kernel_size, kernel_size, kernel_size};
+  LNCC_ENTRY(impl_lncc_loss_map_backward(grad_map, pred, target, dtype, B, D, H, W, win, smooth_dr, grad, scratch,
+                                         scratch_bytes, stream),
+             stream);
+}
+
+int lncc_aniso_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H, int64_t W,
+                       int kd, int kh, int kw, float smooth_dr, void* grad, float grad_scale,
+                       const float* grad_scale_dev, double* cc_sum_out, float* loss_out, double loss_count,
+                       void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  const Win win{kd, kh, kw};
+  LNCC_ENTRY(impl_lncc_aniso_forward(pred, target, dtype, B, D, H, W, win, smooth_dr, grad, grad_scale, grad_scale_dev,
+                                     cc_sum_out, loss_out, loss_count, scratch, scratch_bytes, stream),
+             stream);
+}
+
+int lncc_aniso_loss_map_forward(const void* pred, const void* target, int dtype, int64_t B, int64_t D, int64_t H,
+                                int64_t W, int kd, int kh, int kw, float smooth_dr, float* loss_map,
+                                cudaStream_t stream) {
+  const Win win{kd, kh, kw};
+  LNCC_ENTRY(impl_lncc_loss_map_forward(pred, target, dtype, B, D, H, W, win, smooth_dr, loss_map, stream), stream);
+}
+
+int lncc_aniso_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype, int64_t B,
+                                 int64_t D, int64_t H, int64_t W, int kd, int kh, int kw, float smooth_dr, void* grad,
+                                 float* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  const Win win{kd, kh, kw};
+  LNCC_ENTRY(impl_lncc_loss_map_backward(grad_map, pred, target, dtype, B, D, H, W, win, smooth_dr, grad, scratch,
+                                         scratch_bytes, stream),
+             stream);
 }
 
 int lncc_scale_grad(void* grad, int dtype, int64_t n, const float* grad_out_dev, cudaStream_t stream) {

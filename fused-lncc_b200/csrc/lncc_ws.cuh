@@ -37,6 +37,7 @@
 
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "lncc_check.cuh"
@@ -121,32 +122,48 @@ __device__ __forceinline__ int swz(int x) {
 __device__ __forceinline__ int swz_chunk(int c) { return ((c & ~7) | ((c & 7) ^ ((c >> 3) & 3))) << 2; }
 
 // ---- element access --------------------------------------------------------------------------------
+// Two packed 16-bit elements (bf16 or fp16, in one 32-bit word) <-> float2.
 template <typename S>
-struct IO;
+struct Pair16;
+template <>
+struct Pair16<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 to2(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  }
+  static __device__ __forceinline__ uint32_t from2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <>
+struct Pair16<__half> {
+  static __device__ __forceinline__ float2 to2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
+  static __device__ __forceinline__ uint32_t from2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <typename S>
+struct IO {  // 16-bit types: four elements in 8 bytes
+  static __device__ __forceinline__ float4 ld(const S* p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = Pair16<S>::to2(u.x), b = Pair16<S>::to2(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void st(S* p, float4 v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(Pair16<S>::from2(v.x, v.y), Pair16<S>::from2(v.z, v.w));
+  }
+};
+
 template <>
 struct IO<float> {
   static __device__ __forceinline__ float4 ld(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
   static __device__ __forceinline__ void st(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 };
-template <>
-struct IO<__nv_bfloat16> {
-  static __device__ __forceinline__ float4 ld(const __nv_bfloat16* p) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-    return make_float4(a.x, a.y, b.x, b.y);
-  }
-  static __device__ __forceinline__ void st(__nv_bfloat16* p, float4 v) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&a);
-    u.y = *reinterpret_cast<uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(p) = u;
-  }
-};
 
 // Chunk of CW = 4 or 8 consecutive elements <-> CW/4 float4. CW = 8 uses one 256-bit access for fp32
-// (ld/st .v8.f32, 32-byte aligned) and one 128-bit access for bf16: with 16 columns per lane, a lane's
+// (ld/st .v8.f32, 32-byte aligned) and one 128-bit access for bf16 / fp16: with 16 columns per lane, a lane's
 // two 8-column chunks fill whole 32-byte sectors, where 4-column chunks fill only half of each.
 template <typename S, int CW>
 struct Chunk;
@@ -155,10 +172,10 @@ struct Chunk<float, 4> {
   static __device__ __forceinline__ void ld(const float* p, float4* o) { o[0] = IO<float>::ld(p); }
   static __device__ __forceinline__ void st(float* p, const float4* v) { IO<float>::st(p, v[0]); }
 };
-template <>
-struct Chunk<__nv_bfloat16, 4> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float4* o) { o[0] = IO<__nv_bfloat16>::ld(p); }
-  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float4* v) { IO<__nv_bfloat16>::st(p, v[0]); }
+template <typename S>
+struct Chunk<S, 4> {  // 16-bit types
+  static __device__ __forceinline__ void ld(const S* p, float4* o) { o[0] = IO<S>::ld(p); }
+  static __device__ __forceinline__ void st(S* p, const float4* v) { IO<S>::st(p, v[0]); }
 };
 template <>
 struct Chunk<float, 8> {
@@ -174,27 +191,17 @@ struct Chunk<float, 8> {
                  : "memory");
   }
 };
-template <>
-struct Chunk<__nv_bfloat16, 8> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float4* o) {
+template <typename S>
+struct Chunk<S, 8> {  // 16-bit types: one 128-bit access
+  static __device__ __forceinline__ void ld(const S* p, float4* o) {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * h]));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * h + 1]));
-      o[h] = make_float4(a.x, a.y, b.x, b.y);
-    }
+    const float2 a = Pair16<S>::to2(u.x), b = Pair16<S>::to2(u.y), c = Pair16<S>::to2(u.z), d = Pair16<S>::to2(u.w);
+    o[0] = make_float4(a.x, a.y, b.x, b.y);
+    o[1] = make_float4(c.x, c.y, d.x, d.y);
   }
-  static __device__ __forceinline__ void st(__nv_bfloat16* p, const float4* v) {
-    uint32_t w[4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      __nv_bfloat162 a = __floats2bfloat162_rn(v[h].x, v[h].y), b = __floats2bfloat162_rn(v[h].z, v[h].w);
-      w[2 * h] = *reinterpret_cast<uint32_t*>(&a);
-      w[2 * h + 1] = *reinterpret_cast<uint32_t*>(&b);
-    }
-    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  static __device__ __forceinline__ void st(S* p, const float4* v) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(Pair16<S>::from2(v[0].x, v[0].y), Pair16<S>::from2(v[0].z, v[0].w),
+                                              Pair16<S>::from2(v[1].x, v[1].y), Pair16<S>::from2(v[1].z, v[1].w));
   }
 };
 

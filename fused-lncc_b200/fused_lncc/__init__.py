@@ -19,11 +19,12 @@ import torch
 
 from . import _lib
 
-__all__ = ["fused_lncc_loss", "lncc_fused", "loss_map", "FusedLNCC", "FusedLNCCMap", "compat"]
+__all__ = ["fused_lncc_loss", "lncc_fused", "loss_map", "FusedLNCC", "FusedLNCCMap", "compat", "window"]
 
 REDUCTIONS = {"mean": 0, "sum": 1}  # the fused kernel's reductions; 'none' has its own path
 
-_DTYPES = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16}
+# fp16 is an addition the reference lists as open (reference BENCHMARKS.md:177-178)
+_DTYPES = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16, torch.float16: _lib.LNCC_F16}
 
 
 def _check_pair(pred, target):
@@ -35,7 +36,7 @@ def _check_pair(pred, target):
     if pred.shape != target.shape or pred.dtype != target.dtype:
         raise RuntimeError("fused_lncc: target must match pred in shape and dtype")
     if pred.dtype not in _DTYPES:
-        raise RuntimeError(f"fused_lncc: float32 or bfloat16 only, got {pred.dtype}")
+        raise RuntimeError(f"fused_lncc: float32, bfloat16 or float16 only, got {pred.dtype}")
     if not (pred.is_contiguous() and target.is_contiguous()):
         raise RuntimeError("fused_lncc: pred and target must be contiguous")
     if pred.dim() < 3:
@@ -47,7 +48,7 @@ def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_s
                out=None):
     """Run the fused kernel once: returns (loss, grad).
 
-    pred/target: contiguous (..., D, H, W) CUDA tensors, fp32 or bf16; the leading dims are
+    pred/target: contiguous (..., D, H, W) CUDA tensors, fp32, bf16 or fp16; the leading dims are
     flattened into B volumes (the reference's N*C reshape, fused_lncc/__init__.py:52-55).
     grad: also produce d/dpred, scaled by grad_scale (default -1/M, i.e. of 1 - mean(cc)).
     loss_count: divisor of the loss (default M = number of voxels produced).
@@ -138,7 +139,8 @@ def _(pred, target, kernel_size, smooth_dr, need_grad, reduction):
 
 
 def loss_map(pred, target, kernel_size=7, smooth_dr=1e-5):
-    """Per-voxel loss 1 - cc (cc clamped to 1, NaN kept), an fp32 tensor of pred's shape."""
+    """Per-voxel loss 1 - cc (cc clamped to 1, NaN kept), an fp32 tensor of pred's shape.
+    kernel_size: an int k (cubic) or a (kd, kh, kw) tuple (non-cubic window)."""
     _check_pair(pred, target)
     *lead, D, H, W = pred.shape
     B = 1
@@ -147,9 +149,13 @@ def loss_map(pred, target, kernel_size=7, smooth_dr=1e-5):
     out = torch.empty(pred.shape, dtype=torch.float32, device=pred.device)
     lib = _lib.load()
     with torch.cuda.device(pred.device):
-        st = lib.lncc_loss_map_forward(pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype], B, D, H, W,
-                                       int(kernel_size), float(smooth_dr), out.data_ptr(),
-                                       torch.cuda.current_stream(pred.device).cuda_stream)
+        stream = torch.cuda.current_stream(pred.device).cuda_stream
+        if isinstance(kernel_size, tuple):  # non-cubic window (kd, kh, kw)
+            st = lib.lncc_aniso_loss_map_forward(pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype], B, D, H,
+                                                 W, *kernel_size, float(smooth_dr), out.data_ptr(), stream)
+        else:
+            st = lib.lncc_loss_map_forward(pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype], B, D, H, W,
+                                           int(kernel_size), float(smooth_dr), out.data_ptr(), stream)
     _lib.check(st, "fused_lncc loss_map")
     return out
 
@@ -169,9 +175,15 @@ def loss_map_backward(grad_map, pred, target, kernel_size=7, smooth_dr=1e-5):
     with torch.cuda.device(pred.device):
         nb = lib.lncc_loss_map_scratch_bytes(B, D, H, W)
         scratch = torch.empty(max(nb, 4) // 4, dtype=torch.float32, device=pred.device)
-        st = lib.lncc_loss_map_backward(gm.data_ptr(), pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype],
-                                        B, D, H, W, int(kernel_size), float(smooth_dr), g.data_ptr(),
-                                        scratch.data_ptr(), nb, torch.cuda.current_stream(pred.device).cuda_stream)
+        stream = torch.cuda.current_stream(pred.device).cuda_stream
+        if isinstance(kernel_size, tuple):  # non-cubic window (kd, kh, kw)
+            st = lib.lncc_aniso_loss_map_backward(gm.data_ptr(), pred.data_ptr(), target.data_ptr(),
+                                                  _DTYPES[pred.dtype], B, D, H, W, *kernel_size, float(smooth_dr),
+                                                  g.data_ptr(), scratch.data_ptr(), nb, stream)
+        else:
+            st = lib.lncc_loss_map_backward(gm.data_ptr(), pred.data_ptr(), target.data_ptr(), _DTYPES[pred.dtype],
+                                            B, D, H, W, int(kernel_size), float(smooth_dr), g.data_ptr(),
+                                            scratch.data_ptr(), nb, stream)
     _lib.check(st, "fused_lncc loss_map_backward")
     return g
 
@@ -197,6 +209,23 @@ def _(grad_map, pred, target, kernel_size, smooth_dr):
     return torch.empty_like(pred)
 
 
+@torch.library.custom_op("fused_lncc::grad_times", mutates_args=())
+def _grad_times_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float, reduction: int,
+                   grad_out: torch.Tensor) -> torch.Tensor:
+    """grad_out * dL/dpred in one fused pass, grad_out folded into the fp32 scale before the gradient is
+    rounded to pred's dtype (fp16: a scaled loss, as with torch.amp.GradScaler, keeps gradients that
+    -1/M alone would flush to zero)."""
+    go = grad_out.detach().to(device=pred.device, dtype=torch.float32).contiguous()
+    scale = -1.0 if reduction == REDUCTIONS["sum"] else None
+    _, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=True, grad_scale=scale, grad_scale_dev=go)
+    return g
+
+
+@_grad_times_op.register_fake
+def _(pred, target, kernel_size, smooth_dr, reduction, grad_out):
+    return torch.empty_like(pred)
+
+
 @torch.library.custom_op("fused_lncc::scale_grad_", mutates_args=("grad",))
 def _scale_grad_op(grad: torch.Tensor, grad_out: torch.Tensor) -> None:
     scale_grad_(grad, grad_out)
@@ -213,6 +242,9 @@ class FusedLNCC(torch.autograd.Function):
     forward: one fused pass -> (loss, dL/dpred for grad_out = 1), the gradient kept for backward.
     backward: scales that gradient by grad_out in place and hands it over (no copy). A second
     backward through the same graph (retain_graph=True) recomputes it from the saved inputs.
+    fp16 inputs: the forward computes the loss only and the backward one fused pass with grad_out
+    applied in fp32 before the fp16 rounding (the gradient, of order 1/M, is below fp16's normal range
+    for large M unless the loss is scaled, as torch.amp.GradScaler does).
     """
 
     @staticmethod
@@ -220,16 +252,22 @@ class FusedLNCC(torch.autograd.Function):
         # Grad mode is off inside forward; the caller passes whether the graph wants d/dpred.
         if need_grad is None:
             need_grad = bool(ctx.needs_input_grad[0])
-        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr, need_grad, reduction)
+        ctx.deferred = need_grad and pred.dtype == torch.float16
+        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr,
+                                                need_grad and not ctx.deferred, reduction)
         ctx.save_for_backward(pred, target)
         ctx.k = kernel_size
         ctx.dr = smooth_dr
         ctx.reduction = reduction
-        ctx.grad = g if need_grad else None
+        ctx.grad = g if need_grad and not ctx.deferred else None
         return loss
 
     @staticmethod
     def backward(ctx, grad_out):
+        if ctx.deferred:
+            pred, target = ctx.saved_tensors
+            g = torch.ops.fused_lncc.grad_times(pred, target, ctx.k, ctx.dr, ctx.reduction, grad_out)
+            return g, None, None, None, None, None
         g = ctx.grad
         ctx.grad = None  # hand the buffer over; a later backward recomputes
         if g is None or g.numel() == 0:
@@ -263,19 +301,26 @@ class FusedLNCCMap(torch.autograd.Function):
 def fused_lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5, reduction="mean"):
     """1 - mean(squared local NCC). Gradient flows through `pred` only.
 
-    pred, target: (N, C, D, H, W) fp32 or bf16 CUDA. kernel_size odd (3, 5, 7 or 9).
+    pred, target: (N, C, D, H, W) fp32, bf16 or fp16 CUDA (fp16 is not in the reference). kernel_size odd (3, 5, 7 or 9),
+    or a (kd, kh, kw) tuple of odd sides 1 .. 9 (a non-cubic window, not in the reference).
     Returns a 0-dim fp32 loss in [0, 1] (reference fused_lncc/__init__.py:77-83).
     reduction (not in the reference, which lists it as open): 'mean' (default, the reference's
     loss), 'sum' (sum of 1 - cc, 0-dim fp32) or 'none' (fp32 map 1 - cc of pred's shape)."""
     assert pred.dim() == 5 and pred.shape == target.shape, "expect matching (N,C,D,H,W)"
-    assert kernel_size % 2 == 1, "kernel_size must be odd"
+    kernel_size = window.window_of(kernel_size)
     if reduction == "none":
+        if isinstance(kernel_size, tuple):
+            return window.FusedLNCCWindowMap.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr)
         return FusedLNCCMap.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr)
     if reduction not in REDUCTIONS:
         raise ValueError(f"fused_lncc: reduction must be 'mean', 'sum' or 'none', got {reduction!r}")
+    if isinstance(kernel_size, tuple):
+        return window.FusedLNCCWindow.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr,
+                                            REDUCTIONS[reduction])
     need_grad = bool(pred.requires_grad and torch.is_grad_enabled())
     return FusedLNCC.apply(pred.contiguous(), target.contiguous(), kernel_size, smooth_dr, need_grad,
                            REDUCTIONS[reduction])
 
 
 from . import compat  # noqa: E402  (registers the reference's fused_lncc::forward/backward ops)
+from . import window  # noqa: E402  (non-cubic windows)

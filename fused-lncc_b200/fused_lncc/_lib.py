@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "liblncc_sm100.so")
 LNCC_OK = 0
 LNCC_F32 = 0
 LNCC_BF16 = 1
+LNCC_F16 = 2
 
 _c_i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
@@ -79,6 +80,24 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_float, _vp, _vp,      # kernel_size, scale, grad, stream
     ]),
     "lncc_box3d": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
+    "lncc_aniso_scratch_bytes": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int]),
+    "lncc_aniso_forward": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int,                      # pred, target, dtype
+        _c_i64, _c_i64, _c_i64, _c_i64,              # B, D, H, W
+        ctypes.c_int, ctypes.c_int, ctypes.c_int,    # kd, kh, kw
+        ctypes.c_float,                              # smooth_dr
+        _vp, ctypes.c_float, _vp,                    # grad, grad_scale, grad_scale_dev
+        _vp, _vp, ctypes.c_double,                   # cc_sum_out, loss_out, loss_count
+        _vp, ctypes.c_size_t, _vp,                   # scratch, bytes, stream
+    ]),
+    "lncc_aniso_loss_map_forward": (ctypes.c_int, [
+        _vp, _vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp,
+    ]),
+    "lncc_aniso_loss_map_backward": (ctypes.c_int, [
+        _vp, _vp, _vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
 }
 
 _lock = threading.Lock()

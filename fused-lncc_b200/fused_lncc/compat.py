@@ -23,7 +23,7 @@ from . import _lib
 
 __all__ = ["lncc_forward", "lncc_backward", "box3d_sep_forward"]
 
-_DT = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16}
+_DT = {torch.float32: _lib.LNCC_F32, torch.bfloat16: _lib.LNCC_BF16, torch.float16: _lib.LNCC_F16}
 
 
 def _check(cond, msg):
@@ -41,7 +41,7 @@ def lncc_forward(P, T, kernel_size, dr):
     _check(P.is_cuda and P.is_contiguous() and P.dim() == 4, "P must be a contiguous 4D CUDA tensor")
     _check(T.is_cuda and T.is_contiguous() and T.shape == P.shape and T.dtype == P.dtype
            and T.device == P.device, "T must match P")
-    _check(P.dtype in _DT, f"fused_lncc: float32 or bfloat16 only, got {P.dtype}")
+    _check(P.dtype in _DT, f"fused_lncc: float32, bfloat16 or float16 only, got {P.dtype}")
     B, D, H, W = P.shape
     maps = [torch.empty(P.shape, dtype=torch.float32, device=P.device) for _ in range(4)]
     if P.numel() == 0:
@@ -65,7 +65,7 @@ def lncc_backward(A, Bc, Cc, P, T, kernel_size, scale):
     _check(P.is_cuda and P.is_contiguous() and P.shape == A.shape and T.is_contiguous()
            and T.shape == A.shape and P.dtype == T.dtype and P.device == A.device
            and T.device == A.device, "P,T must match A shape")
-    _check(P.dtype in _DT, f"fused_lncc: float32 or bfloat16 only, got {P.dtype}")
+    _check(P.dtype in _DT, f"fused_lncc: float32, bfloat16 or float16 only, got {P.dtype}")
     B, D, H, W = A.shape
     g = torch.empty_like(P)
     if P.numel() == 0:

@@ -11,7 +11,8 @@
  * events) on its first such call, forked from and joined back into the caller's stream. To keep every
  * launch on the caller's stream, call lncc_set_companion(0) or use lncc_fused_forward_noalloc.
  *
- * Layout: pred/target/grad are contiguous (B, D, H, W) volumes, B = N*C, W fastest, fp32 or bf16.
+ * Layout: pred/target/grad are contiguous (B, D, H, W) volumes, B = N*C, W fastest, fp32, bf16 or
+ * fp16 (every type is loaded into fp32 registers; all arithmetic is fp32, the loss sum fp64).
  *
  * Math (reference fused_lncc/csrc/lncc3d.cu:5-8,93-108): for each voxel the k^3 zero-padded box
  * (n = k^3 at borders too) gives Sp, St, Spp, Stt, Spt;
@@ -36,7 +37,7 @@ enum lncc_status {
   LNCC_OK = 0,
   LNCC_ERR_BAD_ARG = 1,         /* null pointer, non-positive size, bad plane range */
   LNCC_ERR_KERNEL_SIZE = 2,     /* kernel_size not in {3,5,7,9}  (lncc3d.cu:123) */
-  LNCC_ERR_DTYPE = 3,           /* dtype not fp32/bf16           (lncc3d.cu:158) */
+  LNCC_ERR_DTYPE = 3,           /* dtype not fp32/bf16/fp16      (lncc3d.cu:158) */
   LNCC_ERR_LAUNCH = 4,          /* kernel launch failed          (lncc3d.cu:159) */
   LNCC_ERR_SMEM = 5,            /* shared memory need above the device opt-in cap (lncc3d.cu:143-148) */
   LNCC_ERR_WORKSPACE = 6,       /* workspace missing or smaller than lncc_workspace_bytes() */
@@ -46,8 +47,10 @@ enum lncc_status {
   LNCC_ERR_CHECK = 10           /* checked build only: a kernel index left its array */
 };
 
-/* Element types of pred / target / grad (the reference dispatches on the same two, lncc3d.cu:151-158). */
-enum lncc_dtype { LNCC_F32 = 0, LNCC_BF16 = 1 };
+/* Element types of pred / target / grad. The reference dispatches on fp32 and bf16 (lncc3d.cu:151-158)
+ * and lists fp16 as open (BENCHMARKS.md:177-178); fp16 is handled exactly like bf16: loaded into
+ * fp32, the gradient rounded to fp16 on store. */
+enum lncc_dtype { LNCC_F32 = 0, LNCC_BF16 = 1, LNCC_F16 = 2 };
 
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* lncc_strerror(int status);
@@ -224,6 +227,38 @@ int lncc_loss_map_backward(const float* grad_map, const void* pred, const void* 
                            int64_t B, int64_t D, int64_t H, int64_t W,
                            int kernel_size, float smooth_dr, void* grad,
                            float* scratch, size_t scratch_bytes, cudaStream_t stream);
+
+/*
+ * Non-cubic windows kd x kh x kw (depth, height, width; each side odd, 1 .. 9; n = kd*kh*kw), a
+ * feature the reference lists as open (BENCHMARKS.md:177-178) and has no entry point for. The window
+ * replaces the k^3 cube everywhere in the math above (zero padding, n counted as the full window at
+ * the borders, the same clamps), so a cubic (k, k, k) gives lncc_fused_forward's results.
+ *
+ * lncc_aniso_forward: every argument as for lncc_fused_forward (whole volumes: no plane range). One
+ * pass writes the adjoint maps (three fp32 maps, only when grad != NULL) and one fp64 cc sum per
+ * thread block into `scratch`; a fixed-order reduction gives cc_sum_out / loss_out; a second pass
+ * boxes the maps into grad = grad_scale * (*grad_scale_dev if not NULL) * d(sum cc)/dpred. scratch:
+ * lncc_aniso_scratch_bytes(B, D, H, W, grad != NULL) bytes, 8-byte aligned (12 bytes per voxel with
+ * the gradient, a few KB without). This path materialises maps, unlike the fused kernel: about 60
+ * bytes of traffic per voxel against 12.
+ * lncc_aniso_loss_map_forward / _backward: lncc_loss_map_forward / _backward for such a window
+ * (reduction 'none'; scratch of lncc_loss_map_scratch_bytes()).
+ * A side outside 1 .. 9 or even returns LNCC_ERR_KERNEL_SIZE.
+ */
+size_t lncc_aniso_scratch_bytes(int64_t B, int64_t D, int64_t H, int64_t W, int with_grad);
+int lncc_aniso_forward(const void* pred, const void* target, int dtype,
+                       int64_t B, int64_t D, int64_t H, int64_t W,
+                       int kd, int kh, int kw, float smooth_dr,
+                       void* grad, float grad_scale, const float* grad_scale_dev,
+                       double* cc_sum_out, float* loss_out, double loss_count,
+                       void* scratch, size_t scratch_bytes, cudaStream_t stream);
+int lncc_aniso_loss_map_forward(const void* pred, const void* target, int dtype,
+                                int64_t B, int64_t D, int64_t H, int64_t W,
+                                int kd, int kh, int kw, float smooth_dr, float* loss_map, cudaStream_t stream);
+int lncc_aniso_loss_map_backward(const float* grad_map, const void* pred, const void* target, int dtype,
+                                 int64_t B, int64_t D, int64_t H, int64_t W,
+                                 int kd, int kh, int kw, float smooth_dr, void* grad,
+                                 float* scratch, size_t scratch_bytes, cudaStream_t stream);
 
 /*
  * Kernel selection for the whole process (diagnostics and cross-checks): 0 = automatic (default:

@@ -36,6 +36,10 @@ def load():
                 lib.oracle_lncc.argtypes = [vp, vp, i64, i64, i64, i64, ctypes.c_int, ctypes.c_double,
                                             i64, i64, vp, vp, ctypes.c_double, vp, vp, vp, vp,
                                             ctypes.c_int]
+                lib.oracle_lncc_win.restype = ctypes.c_int
+                lib.oracle_lncc_win.argtypes = [vp, vp, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int, ctypes.c_double, i64, i64, vp, vp,
+                                                ctypes.c_double, vp, vp, vp, vp, ctypes.c_int]
                 lib.oracle_box3d.restype = ctypes.c_int
                 lib.oracle_box3d.argtypes = [vp, vp, i64, i64, i64, i64, ctypes.c_int]
                 lib.oracle_num_threads.restype = ctypes.c_int
@@ -55,7 +59,12 @@ def lncc(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, z_range=None
 
     Returns dict(loss, cc_sum, count, grad (or None), and with maps=True ncc, A, B, C).
     grad is grad_scale * d(sum cc)/dpred (default -1/M: the gradient of 1 - mean(cc)).
+    kernel_size: an odd int (the reference's cubic window) or a (kd, kh, kw) tuple of odd sides.
     """
+    if isinstance(kernel_size, (tuple, list)):
+        kd, kh, kw = (int(v) for v in kernel_size)
+    else:
+        kd = kh = kw = int(kernel_size)
     p = _f32(pred)
     t = _f32(target)
     assert p.shape == t.shape and p.ndim >= 3
@@ -72,7 +81,7 @@ def lncc(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, z_range=None
             mp[name] = np.empty(p.shape, np.float32)
     s = ctypes.c_double(0.0)
     ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
-    rc = load().oracle_lncc(ptr(p), ptr(t), B, D, H, W, int(kernel_size), float(smooth_dr), z0, z1,
+    rc = load().oracle_lncc_win(ptr(p), ptr(t), B, D, H, W, kd, kh, kw, float(smooth_dr), z0, z1,
                             ctypes.cast(ctypes.byref(s), ctypes.c_void_p), ptr(g), float(grad_scale),
                             ptr(mp.get("ncc")), ptr(mp.get("A")), ptr(mp.get("B")), ptr(mp.get("C")),
                             1 if direct else 0)

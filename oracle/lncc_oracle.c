@@ -51,21 +51,24 @@ static void box_axis(const double* x, double* y, int64_t n0, int64_t n1, int64_t
   }
 }
 
-static void box3(const double* x, double* y, double* tmp, int64_t D, int64_t H, int64_t W, int r) {
-  box_axis(x, y, D, H, W, 2, r);
-  box_axis(y, tmp, D, H, W, 1, r);
-  box_axis(tmp, y, D, H, W, 0, r);
+/* Half-widths of the window along D, H, W (a cubic window has rd = rh = rw = k/2). */
+typedef struct { int rd, rh, rw; } Radii;
+
+static void box3(const double* x, double* y, double* tmp, int64_t D, int64_t H, int64_t W, Radii r) {
+  box_axis(x, y, D, H, W, 2, r.rw);
+  box_axis(y, tmp, D, H, W, 1, r.rh);
+  box_axis(tmp, y, D, H, W, 0, r.rd);
 }
 
 /* Direct (non-prefix) box for accuracy on the golden vectors: sum of the window, in double. */
-static void box3_direct(const double* x, double* y, double* tmp, int64_t D, int64_t H, int64_t W, int r) {
+static void box3_direct(const double* x, double* y, double* tmp, int64_t D, int64_t H, int64_t W, Radii rr) {
   const int64_t HW = H * W;
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < D * HW; ++i) {
     int64_t w = i % W, h = (i / W) % H, z = i / HW;
     (void)z; (void)h;
     double s = 0.0;
-    for (int64_t d = -r; d <= r; ++d) {
+    for (int64_t d = -rr.rw; d <= rr.rw; ++d) {
       int64_t ww = w + d;
       if (ww >= 0 && ww < W) s += x[i + d];
     }
@@ -75,7 +78,7 @@ static void box3_direct(const double* x, double* y, double* tmp, int64_t D, int6
   for (int64_t i = 0; i < D * HW; ++i) {
     int64_t h = (i / W) % H;
     double s = 0.0;
-    for (int64_t d = -r; d <= r; ++d) {
+    for (int64_t d = -rr.rh; d <= rr.rh; ++d) {
       int64_t hh = h + d;
       if (hh >= 0 && hh < H) s += tmp[i + d * W];
     }
@@ -85,7 +88,7 @@ static void box3_direct(const double* x, double* y, double* tmp, int64_t D, int6
   for (int64_t i = 0; i < D * HW; ++i) {
     int64_t z = i / HW;
     double s = 0.0;
-    for (int64_t d = -r; d <= r; ++d) {
+    for (int64_t d = -rr.rd; d <= rr.rd; ++d) {
       int64_t zz = z + d;
       if (zz >= 0 && zz < D) s += y[i + d * HW];
     }
@@ -95,7 +98,7 @@ static void box3_direct(const double* x, double* y, double* tmp, int64_t D, int6
 }
 
 static void do_box(int direct, const double* x, double* y, double* tmp, int64_t D, int64_t H, int64_t W,
-                   int r) {
+                   Radii r) {
   if (direct) box3_direct(x, y, tmp, D, H, W, r);
   else box3(x, y, tmp, D, H, W, r);
 }
@@ -110,13 +113,19 @@ static void do_box(int direct, const double* x, double* y, double* tmp, int64_t 
  *   direct         : 1 = direct window sums, 0 = prefix-sum differences (faster).
  * Returns 0, or -1 on bad arguments / allocation failure.
  */
-int oracle_lncc(const float* p, const float* t, int64_t B, int64_t D, int64_t H, int64_t W, int k,
-                double dr, int64_t z_begin, int64_t z_end, double* cc_sum, float* grad, double grad_scale,
-                float* ncc, float* A_out, float* B_out, float* C_out, int direct) {
-  if (!p || !t || B < 1 || D < 1 || H < 1 || W < 1 || k < 1 || (k % 2) == 0) return -1;
+/*
+ * As oracle_lncc for a kd x kh x kw window (each side odd): the same math with n = kd*kh*kw. The
+ * reference has cubic windows only; this serves the non-cubic windows its roadmap lists as open
+ * (BENCHMARKS.md:177-178).
+ */
+int oracle_lncc_win(const float* p, const float* t, int64_t B, int64_t D, int64_t H, int64_t W, int kd, int kh,
+                    int kw, double dr, int64_t z_begin, int64_t z_end, double* cc_sum, float* grad,
+                    double grad_scale, float* ncc, float* A_out, float* B_out, float* C_out, int direct) {
+  if (!p || !t || B < 1 || D < 1 || H < 1 || W < 1) return -1;
+  if (kd < 1 || kh < 1 || kw < 1 || (kd % 2) == 0 || (kh % 2) == 0 || (kw % 2) == 0) return -1;
   if (z_begin < 0 || z_end > D || z_end <= z_begin) return -1;
-  const int r = k / 2;
-  const double n = (double)k * k * k;
+  const Radii r = {kd / 2, kh / 2, kw / 2};
+  const double n = (double)kd * kh * kw;
   const int64_t V = D * H * W, HW = H * W;
   double* f[5];
   double* adj[3];
@@ -190,6 +199,13 @@ int oracle_lncc(const float* p, const float* t, int64_t B, int64_t D, int64_t H,
   return ok ? 0 : -1;
 }
 
+int oracle_lncc(const float* p, const float* t, int64_t B, int64_t D, int64_t H, int64_t W, int k,
+                double dr, int64_t z_begin, int64_t z_end, double* cc_sum, float* grad, double grad_scale,
+                float* ncc, float* A_out, float* B_out, float* C_out, int direct) {
+  return oracle_lncc_win(p, t, B, D, H, W, k, k, k, dr, z_begin, z_end, cc_sum, grad, grad_scale, ncc, A_out,
+                         B_out, C_out, direct);
+}
+
 /* Zero-padded k^3 box sum of one fp32 field (reference box3d_sep_forward, lncc3d.cu:287-344). */
 int oracle_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int64_t W, int k) {
   if (!x || !y || B < 1 || D < 1 || H < 1 || W < 1 || k < 1 || (k % 2) == 0) return -1;
@@ -200,7 +216,8 @@ int oracle_box3d(const float* x, float* y, int64_t B, int64_t D, int64_t H, int6
   if (!a || !o || !tmp) { free(a); free(o); free(tmp); return -1; }
   for (int64_t b = 0; b < B; ++b) {
     for (int64_t i = 0; i < V; ++i) a[i] = x[b * V + i];
-    box3_direct(a, o, tmp, D, H, W, k / 2);
+    const Radii rr = {k / 2, k / 2, k / 2};
+    box3_direct(a, o, tmp, D, H, W, rr);
     for (int64_t i = 0; i < V; ++i) y[b * V + i] = (float)o[i];
   }
   free(a); free(o); free(tmp);

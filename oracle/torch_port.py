@@ -10,10 +10,16 @@ import torch
 import torch.nn.functional as F
 
 
+def _sides(k):
+    return tuple(int(v) for v in k) if isinstance(k, (tuple, list)) else (int(k),) * 3
+
+
 def box_dense(x, k):
-    """k^3 zero-padded box as one grouped conv3d (reference torch_lncc.py:12-14)."""
+    """k^3 zero-padded box as one grouped conv3d (reference torch_lncc.py:12-14). k may also be a
+    (kd, kh, kw) tuple: the non-cubic window the reference lists as open, same convolution."""
     ch = x.shape[1]
-    return F.conv3d(x, x.new_ones(ch, 1, k, k, k), padding=k // 2, groups=ch)
+    kd, kh, kw = _sides(k)
+    return F.conv3d(x, x.new_ones(ch, 1, kd, kh, kw), padding=(kd // 2, kh // 2, kw // 2), groups=ch)
 
 
 def box_separable(x, k):
@@ -27,7 +33,8 @@ def box_separable(x, k):
 
 def lncc_loss(pred, target, kernel_size=7, smooth_dr=1e-5, box=box_dense):
     """1 - mean(cc) with autograd (reference torch_lncc.py:25-32)."""
-    n = kernel_size ** 3
+    kd, kh, kw = _sides(kernel_size)
+    n = kd * kh * kw
     sp, st = box(pred, kernel_size), box(target, kernel_size)
     cross = box(pred * target, kernel_size) - sp * st / n
     var_p = box(pred * pred, kernel_size) - sp * sp / n + smooth_dr

@@ -80,7 +80,7 @@ def _call(lib, **kw):
 
 @pytest.mark.parametrize("kw,status", [
     (dict(k=4), 2), (dict(k=11), 2), (dict(k=1), 2),            # lncc3d.cu:123
-    (dict(dtype=2), 3),                                         # lncc3d.cu:158
+    (dict(dtype=3), 3), (dict(dtype=-1), 3),                    # lncc3d.cu:158 (2 = fp16 is accepted)
     (dict(pred=None), 1), (dict(B=0), 1), (dict(z0=3, z1=3), 1), (dict(z1=9), 1),
     (dict(pred=2), 1),                                          # misaligned fp32 pointer
 ])

@@ -94,3 +94,22 @@ def test_reduction_ops_registered_with_fakes():
         assert g.dtype == torch.bfloat16 and g.shape == p.shape
         loss, g2 = torch.ops.fused_lncc.fwd_grad(p, p, 7, 1e-5, True, 1)
         assert loss.dim() == 0 and g2.shape == p.shape
+
+
+def test_window_argument_checks():
+    from fused_lncc.window import window_of
+    assert window_of(7) == 7 and window_of((7, 7, 7)) == 7 and window_of([3, 5, 7]) == (3, 5, 7)
+    assert window_of((1, 1, 1)) == (1, 1, 1)  # not a reference size: the window path takes it
+    for bad in [(3, 4, 3), (3, 3), (3, 3, 3, 3), 6]:
+        with pytest.raises(AssertionError):
+            window_of(bad)
+
+
+def test_window_ops_registered_with_fakes():
+    import torch
+    import fused_lncc  # noqa: F401
+    for name in ("aniso_loss", "aniso_grad", "aniso_loss_map", "aniso_loss_map_backward", "grad_times"):
+        assert hasattr(torch.ops.fused_lncc, name), name
+    p = torch.empty(1, 1, 4, 4, 4, dtype=torch.float16, device="meta")
+    assert torch.ops.fused_lncc.aniso_loss(p, p, 3, 5, 7, 1e-5, 0).dtype == torch.float32
+    assert torch.ops.fused_lncc.aniso_grad(p, p, 3, 5, 7, 1e-5, 0, p.new_empty((), dtype=torch.float32)).dtype == torch.float16

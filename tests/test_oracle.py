@@ -98,3 +98,25 @@ def test_oracle_rejects_bad_args():
         c_oracle.lncc(x, x, 4)
     with pytest.raises(ValueError):
         c_oracle.lncc(x, x, 3, z_range=(2, 2))
+
+
+@pytest.mark.parametrize("win", [(3, 5, 7), (1, 7, 3), (9, 1, 5)])
+def test_oracle_window_matches_conv_port(win):
+    """The oracle's non-cubic window path (no reference counterpart) against the PyTorch port's grouped
+    conv3d with a kd x kh x kw kernel, in fp64 through autograd; the data keep every variance positive,
+    where the port (no variance clamp, as the reference's baseline) and the oracle agree."""
+    g = torch.Generator().manual_seed(sum(win))
+    p = torch.rand(1, 2, 9, 11, 13, generator=g, dtype=torch.float64)
+    t = 0.5 * p + 0.5 * torch.rand(1, 2, 9, 11, 13, generator=g, dtype=torch.float64)
+    o = c_oracle.lncc(p.float().numpy(), t.float().numpy(), win)
+    # the oracle reads fp32 inputs: compare it with the port on the same fp32-rounded values
+    pf = p.float().double().requires_grad_(True)
+    lf = torch_port.lncc_dense(pf, t.float().double(), win)
+    lf.backward()
+    assert abs(o["loss"] - lf.item()) < 1e-10
+    ref = pf.grad.numpy()
+    assert np.linalg.norm(o["grad"] - ref) / np.linalg.norm(ref) < 1e-6
+    # a cubic tuple is the cubic window
+    oc = c_oracle.lncc(p.float().numpy(), t.float().numpy(), (5, 5, 5))
+    ok = c_oracle.lncc(p.float().numpy(), t.float().numpy(), 5)
+    assert abs(oc["loss"] - ok["loss"]) < 1e-12 and np.allclose(oc["grad"], ok["grad"], rtol=1e-6, atol=1e-12)

@@ -455,6 +455,7 @@ def test_ws_companion_two_host_threads():
         ref.append((s.clone(), g.clone()))
     torch.cuda.synchronize()
     errors = []
+    capture_lock = threading.Lock()
 
     def work(idx):
         try:
@@ -470,8 +471,12 @@ def test_ws_companion_two_host_threads():
                         errors.append((idx, "eager"))
                 stream.synchronize()
                 graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-                    lncc_fused(p, t, 7, cc_sum_out=s, out=g)
+                # torch.cuda.graph() empties the allocator cache and synchronises the device on entry,
+                # which CUDA refuses while the other thread's capture is open: one capture at a time
+                # (the other thread's eager calls and replays still run alongside)
+                with capture_lock:
+                    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+                        lncc_fused(p, t, 7, cc_sum_out=s, out=g)
                 for _ in range(4):
                     s.zero_()
                     g.zero_()
