@@ -985,16 +985,28 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
 #pragma unroll
           for (int f = 0; f < 3; ++f) {
             const uint32_t ring = tm + Geo<R>::TM_RING + uint32_t(48 * slot + 16 * f);
-            float old[16], sum[16];
-            if (it >= K) tm_ld16(ring, old);  // the boxed plane leaving the D window
-            else {
+            uint32_t uo[16], us[16];
+            if (it >= K) {
+              tm_ld16_issue(ring, uo);  // the boxed plane leaving the D window
+            } else {
 #pragma unroll
-              for (int m = 0; m < 16; ++m) old[m] = 0.f;
+              for (int m = 0; m < 16; ++m) uo[m] = 0u;
             }
-            if (it > 0) tm_ld16(tsum + uint32_t(16 * f), sum);
-            else {
+            if (it > 0) {
+              tm_ld16_issue(tsum + uint32_t(16 * f), us);
+            } else {
 #pragma unroll
-              for (int m = 0; m < 16; ++m) sum[m] = 0.f;
+              for (int m = 0; m < 16; ++m) us[m] = 0u;
+            }
+            // one wait covers both loads; the second names the other registers so that their uses
+            // follow it
+            tm_wait_ld16(us);
+            tm_wait_ld16(uo);
+            float old[16], sum[16];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              old[m] = __uint_as_float(uo[m]);
+              sum[m] = __uint_as_float(us[m]);
             }
             if (cvalid) {
               box_ah(i, f, [&](int j, float4 w4) {
@@ -1020,9 +1032,21 @@ __global__ void __launch_bounds__(NT, 1) lncc_ws_kernel(const Args a) {
           if (it >= 2 * R) {  // warp-uniform: the TMEM loads below are warp-collective
             tm_wait_st();
             float sa[16], sb[16], sc[16];
-            tm_ld16(tsum, sa);
-            tm_ld16(tsum + 16u, sb);
-            tm_ld16(tsum + 32u, sc);
+            {
+              uint32_t ua[16], ub[16], uc[16];
+              tm_ld16_issue(tsum, ua);
+              tm_ld16_issue(tsum + 16u, ub);
+              tm_ld16_issue(tsum + 32u, uc);
+              tm_wait_ld16(ua);
+              tm_wait_ld16(ub);
+              tm_wait_ld16(uc);
+#pragma unroll
+              for (int m = 0; m < 16; ++m) {
+                sa[m] = __uint_as_float(ua[m]);
+                sb[m] = __uint_as_float(ub[m]);
+                sc[m] = __uint_as_float(uc[m]);
+              }
+            }
             if (out_ok) {
               S* gp = G + int64_t(o - a.z_begin) * HW + roff;
               constexpr int Q = CW / 4;
