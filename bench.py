@@ -197,6 +197,7 @@ def _cpu_model():
 
 
 REFERENCE_MAX_STEPS = 40  # bounds the CPU arm at ~1 s per step
+REFERENCE_MAX_WARMUP = 3
 
 
 def run_reference(args, rank, world):
@@ -205,13 +206,13 @@ def run_reference(args, rank, world):
     from fused_lncc import synth  # noqa: F401  (inputs only)
     pred, target, k, dtype = make_inputs(args.workload, "cpu")
     steps = max(1, min(args.steps, REFERENCE_MAX_STEPS))
-    value, info = cpu_reference_sample(pred, target, k, steps, max(1, min(args.warmup, 1)),
-                                       sample_volumes=args.cpu_sample_volumes)
+    warmup = max(1, min(args.warmup, REFERENCE_MAX_WARMUP))
+    value, info = cpu_reference_sample(pred, target, k, steps, warmup, sample_volumes=args.cpu_sample_volumes)
     shape = WORKLOADS[args.workload][0]
     line = {
         "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "Gvoxel/s", "n_gpus": world,
-        "steps": steps, "warmup": max(1, min(args.warmup, 1)),
-        "ms_per_step": info["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "steps": steps, "warmup": warmup,
+        "ms_per_step": info["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "shape": list(shape), "kernel_size": k,
                    "input_dtype": dtype, "sample_volumes": args.cpu_sample_volumes},
@@ -220,8 +221,8 @@ def run_reference(args, rank, world):
                          "cpu_model": info["cpu_model"]},
         "e2e": {"value": value, "unit": "Gvoxel/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         # each step is a per-voxel rate measured on sample_volumes of the workload's volumes; at most
-        # REFERENCE_MAX_STEPS steps are timed
-        "steps_requested": args.steps,
+        # REFERENCE_MAX_STEPS steps after at most REFERENCE_MAX_WARMUP warm-up steps are timed
+        "steps_requested": args.steps, "warmup_requested": args.warmup,
     }
     print(json.dumps(line), flush=True)
     return 0
