@@ -15,6 +15,8 @@ The backward is then one tiny launch that returns immediately when grad_out == 1
 instead materialises four fp32 maps in the forward and box-sums them again in the backward
 (reference fused_lncc/__init__.py:50-74).
 """
+import contextlib
+
 import torch
 
 from . import _lib
@@ -43,6 +45,18 @@ def _check_pair(pred, target):
         raise RuntimeError("fused_lncc: expect (..., D, H, W) volumes")
 
 
+# Workspace bytes per call shape, so that a step makes one C call instead of two. The size also
+# depends on the process-wide switches (companion launch, kernel choice): a call that finds the cached
+# size too small asks the library again once.
+_WS_BYTES = {}
+
+
+def _on_device(dev):
+    """torch.cuda.device(dev), or nothing when dev is already current (the common case, and the switch
+    costs microseconds that matter for small calls)."""
+    return contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+
+
 def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_scale=None,
                loss_count=None, z_range=None, cc_sum_out=None, loss_out=None, grad_scale_dev=None,
                out=None):
@@ -68,11 +82,17 @@ def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_s
     lib = _lib.load()
     dt = _DTYPES[pred.dtype]
     dev = pred.device
-    with torch.cuda.device(dev):
-        ws_bytes = lib.lncc_workspace_bytes(B, D, H, W, int(kernel_size), dt, z0, z1)
-        if ws_bytes == 0:
-            # invalid size/k/range: let the main call produce the precise status
-            ws_bytes = 8
+    with _on_device(dev):
+        key = (B, D, H, W, int(kernel_size), dt, z0, z1)
+        ws_bytes = _WS_BYTES.get(key)
+        if ws_bytes is None:
+            ws_bytes = lib.lncc_workspace_bytes(B, D, H, W, int(kernel_size), dt, z0, z1)
+            if ws_bytes == 0:
+                # invalid size/k/range: let the main call produce the precise status
+                ws_bytes = 8
+            if len(_WS_BYTES) > 4096:
+                _WS_BYTES.clear()
+            _WS_BYTES[key] = ws_bytes
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         g = None
         if grad:
@@ -91,12 +111,20 @@ def lncc_fused(pred, target, kernel_size=7, smooth_dr=1e-5, *, grad=True, grad_s
         if loss_count is None:
             loss_count = float(max(nout, 1))
         stream = torch.cuda.current_stream(dev).cuda_stream
-        st = lib.lncc_fused_forward(
-            pred.data_ptr(), target.data_ptr(), dt, B, D, H, W, int(kernel_size), float(smooth_dr),
-            z0, z1, g.data_ptr() if g is not None else None, float(grad_scale),
-            grad_scale_dev.data_ptr() if grad_scale_dev is not None else None,
-            cc_sum_out.data_ptr() if cc_sum_out is not None else None, loss_out.data_ptr(),
-            float(loss_count), ws.data_ptr(), ws_bytes, stream)
+
+        def call():
+            return lib.lncc_fused_forward(
+                pred.data_ptr(), target.data_ptr(), dt, B, D, H, W, int(kernel_size), float(smooth_dr),
+                z0, z1, g.data_ptr() if g is not None else None, float(grad_scale),
+                grad_scale_dev.data_ptr() if grad_scale_dev is not None else None,
+                cc_sum_out.data_ptr() if cc_sum_out is not None else None, loss_out.data_ptr(),
+                float(loss_count), ws.data_ptr(), ws_bytes, stream)
+        st = call()
+        if st == _lib.LNCC_ERR_WORKSPACE:  # a switch changed the plan since the size was cached
+            ws_bytes = max(8, lib.lncc_workspace_bytes(B, D, H, W, int(kernel_size), dt, z0, z1))
+            _WS_BYTES[key] = ws_bytes
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            st = call()
     _lib.check(st, "fused_lncc forward")
     return loss_out, g
 
@@ -107,17 +135,18 @@ def scale_grad_(grad, grad_out):
     go = grad_out.detach()
     if go.dtype != torch.float32 or not go.is_contiguous() or go.device != grad.device:
         go = go.to(device=grad.device, dtype=torch.float32).contiguous()
-    with torch.cuda.device(grad.device):
+    with _on_device(grad.device):
         st = lib.lncc_scale_grad(grad.data_ptr(), _DTYPES[grad.dtype], grad.numel(), go.data_ptr(),
                                  torch.cuda.current_stream(grad.device).cuda_stream)
     _lib.check(st, "fused_lncc scale_grad")
 
 
 # torch.library custom ops, so torch.compile traces through without graph breaks (the reference
-# registers fused_lncc::forward/backward for the same reason, fused_lncc/__init__.py:22-46).
-@torch.library.custom_op("fused_lncc::fwd_grad", mutates_args=())
-def _fwd_grad_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float,
-                 need_grad: bool, reduction: int) -> tuple[torch.Tensor, torch.Tensor]:
+# registers fused_lncc::forward/backward for the same reason, fused_lncc/__init__.py:22-46). In eager
+# mode the autograd glue calls the same Python functions directly: the dispatcher round trip of a
+# custom op costs tens of microseconds per call, as much as the kernel of a small call.
+def _fwd_grad_impl(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float,
+                   need_grad: bool, reduction: int) -> tuple[torch.Tensor, torch.Tensor]:
     if reduction == REDUCTIONS["sum"]:
         # sum(1 - cc) = M - sum(cc): the gradient of -sum(cc), the loss from the fp64 cc sum
         cs = torch.empty((), dtype=torch.float64, device=pred.device)
@@ -129,6 +158,9 @@ def _fwd_grad_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smo
     if g is None:
         g = pred.new_empty((0,))
     return loss, g
+
+
+_fwd_grad_op = torch.library.custom_op("fused_lncc::fwd_grad", mutates_args=())(_fwd_grad_impl)
 
 
 @_fwd_grad_op.register_fake
@@ -209,9 +241,8 @@ def _(grad_map, pred, target, kernel_size, smooth_dr):
     return torch.empty_like(pred)
 
 
-@torch.library.custom_op("fused_lncc::grad_times", mutates_args=())
-def _grad_times_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float, reduction: int,
-                   grad_out: torch.Tensor) -> torch.Tensor:
+def _grad_times_impl(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, smooth_dr: float, reduction: int,
+                     grad_out: torch.Tensor) -> torch.Tensor:
     """grad_out * dL/dpred in one fused pass, grad_out folded into the fp32 scale before the gradient is
     rounded to pred's dtype (fp16: a scaled loss, as with torch.amp.GradScaler, keeps gradients that
     -1/M alone would flush to zero)."""
@@ -219,6 +250,9 @@ def _grad_times_op(pred: torch.Tensor, target: torch.Tensor, kernel_size: int, s
     scale = -1.0 if reduction == REDUCTIONS["sum"] else None
     _, g = lncc_fused(pred, target, kernel_size, smooth_dr, grad=True, grad_scale=scale, grad_scale_dev=go)
     return g
+
+
+_grad_times_op = torch.library.custom_op("fused_lncc::grad_times", mutates_args=())(_grad_times_impl)
 
 
 @_grad_times_op.register_fake
@@ -253,8 +287,8 @@ class FusedLNCC(torch.autograd.Function):
         if need_grad is None:
             need_grad = bool(ctx.needs_input_grad[0])
         ctx.deferred = need_grad and pred.dtype == torch.float16
-        loss, g = torch.ops.fused_lncc.fwd_grad(pred, target, kernel_size, smooth_dr,
-                                                need_grad and not ctx.deferred, reduction)
+        fwd = torch.ops.fused_lncc.fwd_grad if torch.compiler.is_compiling() else _fwd_grad_impl
+        loss, g = fwd(pred, target, kernel_size, smooth_dr, need_grad and not ctx.deferred, reduction)
         ctx.save_for_backward(pred, target)
         ctx.k = kernel_size
         ctx.dr = smooth_dr
@@ -264,16 +298,22 @@ class FusedLNCC(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
+        compiling = torch.compiler.is_compiling()
         if ctx.deferred:
             pred, target = ctx.saved_tensors
-            g = torch.ops.fused_lncc.grad_times(pred, target, ctx.k, ctx.dr, ctx.reduction, grad_out)
+            gt = torch.ops.fused_lncc.grad_times if compiling else _grad_times_impl
+            g = gt(pred, target, ctx.k, ctx.dr, ctx.reduction, grad_out)
             return g, None, None, None, None, None
         g = ctx.grad
         ctx.grad = None  # hand the buffer over; a later backward recomputes
         if g is None or g.numel() == 0:
             pred, target = ctx.saved_tensors
-            _, g = torch.ops.fused_lncc.fwd_grad(pred, target, ctx.k, ctx.dr, True, ctx.reduction)
-        torch.ops.fused_lncc.scale_grad_(g, grad_out)
+            fwd = torch.ops.fused_lncc.fwd_grad if compiling else _fwd_grad_impl
+            _, g = fwd(pred, target, ctx.k, ctx.dr, True, ctx.reduction)
+        if compiling:
+            torch.ops.fused_lncc.scale_grad_(g, grad_out)
+        else:
+            scale_grad_(g, grad_out)
         return g, None, None, None, None, None
 
 

@@ -13,6 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "liblncc_sm100.so")
 
 LNCC_OK = 0
+LNCC_ERR_WORKSPACE = 6
 LNCC_F32 = 0
 LNCC_BF16 = 1
 LNCC_F16 = 2

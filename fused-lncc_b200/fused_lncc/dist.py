@@ -85,9 +85,11 @@ _PEER_ERR = {}  # why a group's exchange could not be built (diagnostics)
 def peer_exchange(group=None):
     """The cached PeerExchange of `group` on the current device, or None when the group is not a
     node-local NCCL group or the buffers cannot be mapped (the caller then all-reduces)."""
+    key = (id(group), torch.cuda.current_device())
+    if key in _PEER:  # every step asks: answer from the cache before querying the group
+        return _PEER[key]
     if not (dist.is_available() and dist.is_initialized()) or dist.get_backend(group) != "nccl":
         return None
-    key = (id(group), torch.cuda.current_device())
     if key not in _PEER:
         px, err = None, None
         try:
