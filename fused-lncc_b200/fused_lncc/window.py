@@ -74,9 +74,10 @@ def aniso_fused(pred, target, window, smooth_dr=1e-5, *, grad=False, grad_scale=
     return loss, g
 
 
-@torch.library.custom_op("fused_lncc::aniso_loss", mutates_args=())
-def _aniso_loss_op(pred: torch.Tensor, target: torch.Tensor, kd: int, kh: int, kw: int, smooth_dr: float,
-                   reduction: int) -> torch.Tensor:
+# Ops for torch.compile; in eager mode the autograd functions call the implementations directly,
+# without the custom-op dispatcher's overhead.
+def _aniso_loss_impl(pred: torch.Tensor, target: torch.Tensor, kd: int, kh: int, kw: int, smooth_dr: float,
+                     reduction: int) -> torch.Tensor:
     if reduction == REDUCE_SUM:
         cs = torch.empty((), dtype=torch.float64, device=pred.device)
         aniso_fused(pred, target, (kd, kh, kw), smooth_dr, cc_sum_out=cs)
@@ -85,18 +86,23 @@ def _aniso_loss_op(pred: torch.Tensor, target: torch.Tensor, kd: int, kh: int, k
     return loss
 
 
+_aniso_loss_op = torch.library.custom_op("fused_lncc::aniso_loss", mutates_args=())(_aniso_loss_impl)
+
+
 @_aniso_loss_op.register_fake
 def _(pred, target, kd, kh, kw, smooth_dr, reduction):
     return pred.new_empty((), dtype=torch.float32)
 
 
-@torch.library.custom_op("fused_lncc::aniso_grad", mutates_args=())
-def _aniso_grad_op(pred: torch.Tensor, target: torch.Tensor, kd: int, kh: int, kw: int, smooth_dr: float,
-                   reduction: int, grad_out: torch.Tensor) -> torch.Tensor:
+def _aniso_grad_impl(pred: torch.Tensor, target: torch.Tensor, kd: int, kh: int, kw: int, smooth_dr: float,
+                     reduction: int, grad_out: torch.Tensor) -> torch.Tensor:
     go = grad_out.detach().to(device=pred.device, dtype=torch.float32).contiguous()
     scale = -1.0 if reduction == REDUCE_SUM else None
     _, g = aniso_fused(pred, target, (kd, kh, kw), smooth_dr, grad=True, grad_scale=scale, grad_scale_dev=go)
     return g
+
+
+_aniso_grad_op = torch.library.custom_op("fused_lncc::aniso_grad", mutates_args=())(_aniso_grad_impl)
 
 
 @_aniso_grad_op.register_fake
@@ -113,12 +119,14 @@ class FusedLNCCWindow(torch.autograd.Function):
         ctx.window = window
         ctx.dr = smooth_dr
         ctx.reduction = reduction
-        return torch.ops.fused_lncc.aniso_loss(pred, target, *window, smooth_dr, reduction)
+        fn = torch.ops.fused_lncc.aniso_loss if torch.compiler.is_compiling() else _aniso_loss_impl
+        return fn(pred, target, *window, smooth_dr, reduction)
 
     @staticmethod
     def backward(ctx, grad_out):
         pred, target = ctx.saved_tensors
-        g = torch.ops.fused_lncc.aniso_grad(pred, target, *ctx.window, ctx.dr, ctx.reduction, grad_out)
+        fn = torch.ops.fused_lncc.aniso_grad if torch.compiler.is_compiling() else _aniso_grad_impl
+        g = fn(pred, target, *ctx.window, ctx.dr, ctx.reduction, grad_out)
         return g, None, None, None, None
 
 
